@@ -1,0 +1,456 @@
+#!/usr/bin/env python
+"""Benchmark: deform_conv2d forward+backward on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one forward + backward pass of one deformable-convolution layer over
+one batch (plus the grad_weight/grad_bias all-reduce over NCCL when N > 1).
+The default workload is the large grouped DCNv2 training step
+(c5_train_bf16: global batch 64, 512->512 channels, 38x38, 3x3, pad 2,
+dilation 2, groups 2, offset groups 4, bf16), strong-scaled: each of N ranks
+takes 64/N samples.  Rank 0 prints one JSON line.
+
+--impl reference times the CPU path that the package's parity tests treat as
+ground truth (torchvision.ops.deform_conv2d on the host cores, fp32) on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "mps-deform-conv_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+from mps_deform_conv.workloads import PROBLEMS, make_inputs  # noqa: E402
+
+METRIC = "deform_conv2d fwd+bwd TFLOP/s & % roofline per B200; samples/s at 1/2/4/8 GPUs"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU path
+def cpu_reference_step(p, inp, threads):
+    """torchvision CPU fwd(+bwd) in fp32 on one sample batch; returns seconds."""
+    from torchvision.ops import deform_conv2d as tv_dc
+    torch.set_num_threads(threads)
+    x = inp["input"].float().requires_grad_(p.training)
+    off = inp["offset"].float().requires_grad_(p.training)
+    w = inp["weight"].float().requires_grad_(p.training)
+    b = inp["bias"].float().requires_grad_(p.training) if inp["bias"] is not None else None
+    m = inp["mask"].float().requires_grad_(p.training) if inp["mask"] is not None else None
+    t0 = time.perf_counter()
+    out = tv_dc(x, off, w, b, stride=(p.stride,) * 2, padding=(p.padding,) * 2,
+                dilation=(p.dilation,) * 2, mask=m)
+    if p.training:
+        out.backward(inp["grad_output"].float())
+    return time.perf_counter() - t0
+
+
+def cpu_sample_batch(p):
+    """Samples per CPU step: about 1-3 s of host work per step."""
+    est = {"c1_dcnv1_fp32": 1, "c2_dcnv2_fp32": 2, "c3a_backbone_bf16": 2,
+           "c3b_backbone_s2_bf16": 2, "c4_video_fp16": 1, "c5_train_bf16": 1}
+    return est.get(p.name, 1)
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    p = PROBLEMS[args.workload]
+    threads = os.cpu_count() or 1
+    nb = cpu_sample_batch(p)
+    inp = make_inputs(p, "cpu", batch=nb, dtype=torch.float32)
+    for _ in range(args.warmup):
+        cpu_reference_step(p, inp, threads)
+    ts = [cpu_reference_step(p, inp, threads) for _ in range(args.steps)]
+    total = sum(ts)
+    samples_s = nb * args.steps / total
+    tflops = p.flops(nb) * args.steps / total / 1e12
+    cpu_model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu_model = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
+    except Exception:
+        pass
+    sample = (f"{nb} sample(s) of {p.name} per step, torchvision.ops.deform_conv2d CPU fp32 "
+              f"fwd{'+bwd' if p.training else ''}, {threads} threads, {cpu_model}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tflops, 6), "unit": "TFLOP/s",
+        "samples_per_s": round(samples_s, 4), "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, workload distributions)",
+        "config": {"workload": p.name, "description": p.description, "global_batch": p.batch,
+                   "sample_batch": nb},
+        "cpu_baseline": {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(tflops, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU path
+def run_ours(args):
+    import mps_deform_conv as mdc
+    from mps_deform_conv import _abi
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    p = PROBLEMS[args.workload]
+    assert p.batch % world == 0, f"global batch {p.batch} not divisible by {world} ranks"
+    nb = p.batch // world
+    peaks = load_peaks()
+    inp = make_inputs(p, dev, batch=nb, batch_offset=rank * nb)
+    stride, pad, dil = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
+    x, off, w, b, m, go = (inp[k] for k in ("input", "offset", "weight", "bias", "mask", "grad_output"))
+    leaves = [t for t in (x, off, w, b, m) if t is not None]
+    if p.training:
+        for t in leaves:
+            t.requires_grad_(True)
+    param_grads_idx = [2] + ([3] if b is not None else [])
+
+    def allreduce_param_grads(grads):
+        if world == 1:
+            return
+        import torch.distributed as dist
+        pg = [grads[i] for i in range(len(grads)) if leaves[i] is w or leaves[i] is b]
+        flat = torch.cat([g.reshape(-1) for g in pg])
+        dist.all_reduce(flat)
+        o = 0
+        for g in pg:
+            g.copy_(flat[o:o + g.numel()].view_as(g))
+            o += g.numel()
+
+    fwd_ev = []
+
+    def step(record=None):
+        out = mdc.deform_conv2d(x, off, w, b, stride, pad, dil, m)
+        if record is not None:
+            record.record()
+        if p.training:
+            grads = torch.autograd.grad(out, leaves, go)
+            allreduce_param_grads(grads)
+            return grads
+        return out
+
+    in_bytes = sum(t.numel() * t.element_size() for t in (x, off, m, go) if t is not None)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if in_bytes < 2 * L2_BYTES else None
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, per-step CUDA events, L2 flushed between steps if inputs are small
+    launches0 = _abi.launch_count()
+    _abi.profile_enable(True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            evs[i][0].record()
+            step(record=evs[i][1])
+            evs[i][2].record()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    _abi.profile_enable(False)
+    launches = _abi.launch_count() - launches0
+    prof = _abi.profile_summary()
+    step_ms = [a.elapsed_time(c) for a, _, c in evs]
+    fwd_ms = [a.elapsed_time(f) for a, f, _ in evs]
+    total_ms = max_over_ranks(sum(step_ms), world)
+    clocks = clk.summary()
+
+    flops_step_job = p.flops(p.batch)          # all ranks together
+    tflops = flops_step_job * args.steps / (total_ms / 1e3) / 1e12
+    samples_s = p.batch * args.steps / (total_ms / 1e3)
+
+    # ---- dominant kernel roofline (per-kernel CUDA events recorded by the library)
+    kern = sorted(prof, key=lambda r: -r[2])
+    roof = None
+    if kern:
+        name, nl, kms = kern[0]
+        avg_s = kms / nl / 1e3
+        rf = kernel_roofline(p, nb, name)
+        if rf["bound"] == "tensor":
+            achieved = rf["per_launch"] / avg_s / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            unit = "TFLOP/s"
+        else:
+            achieved = rf["per_launch"] / avg_s / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        roof = {"kernel": name, "bound": rf["bound"], "achieved": round(achieved, 2),
+                "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+                "traffic": args.traffic_per_launch, "avg_launch_ms": round(kms / nl, 4),
+                "launches": nl, "peak_source": peaks["source"] + (" (sustained bf16)" if unit == "TFLOP/s" else ""),
+                "algorithmic_per_launch": rf["per_launch"], "note": rf["note"]}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(p, inp, args, dev, world, allreduce_param_grads, leaves)
+
+    # ---- CPU baseline on rank 0 at N=1
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(p)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s",
+            "samples_per_s": round(samples_s, 2), "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[p.dtype],
+            "data": "synthetic (seeded; workload distributions)",
+            "config": {"workload": p.name, "description": p.description, "global_batch": p.batch,
+                       "per_gpu_batch": nb, "parallelism": f"batch-sharded dp{world}",
+                       "l2": "flushed between steps (256 MB write)" if flush is not None
+                       else f"inputs {in_bytes / 2**20:.0f} MB per rank > L2",
+                       "fwd_ms_per_step": round(sum(fwd_ms) / args.steps, 4)},
+            "roofline": roof,
+            "kernels": [{"name": n, "launches": l, "ms": round(t, 4)} for n, l, t in kern],
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "tensor_cores": bool(mdc._get_lib().uses_tensor_cores(
+                x, w, p.stride, p.stride, p.padding, p.padding, p.dilation, p.dilation,
+                p.groups, p.offset_groups, p.use_mask)),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def kernel_roofline(p, nb, name):
+    """Algorithmic work per launch of a named kernel, for nb samples per launch."""
+    ho, wo = p.out_hw
+    f = p.flops_forward(nb)
+    es = torch.tensor([], dtype=p.dtype).element_size()
+    t = p.kernel * p.kernel
+    if "fwd" in name:
+        return {"bound": "tensor", "per_launch": f, "note": "2*Co*K_red*P forward FLOPs"}
+    if "dgrad" in name or "wgrad" in name:
+        return {"bound": "tensor", "per_launch": f, "note": "2*Co*K_red*P FLOPs (one backward GEMM)"}
+    # gather / scatter kernels: HBM-bound, unique bytes
+    x = nb * p.in_channels * p.height * p.width * es
+    off = nb * 2 * p.offset_groups * t * ho * wo * es
+    msk = nb * p.offset_groups * t * ho * wo * es if p.use_mask else 0
+    return {"bound": "hbm", "per_launch": x + off + msk, "note": "input+offset+mask bytes"}
+
+
+def run_e2e(p, inp, args, dev, world, allreduce_param_grads, leaves):
+    """Same step through the public API, inputs copied from pinned host memory
+    every step and the parameter gradients read back to the host."""
+    import mps_deform_conv as mdc
+    host = {k: (v.detach().cpu().pin_memory() if v is not None else None) for k, v in inp.items()}
+    stride, pad, dil = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
+    dev_w = inp["weight"].detach().clone().requires_grad_(p.training)
+    dev_b = inp["bias"].detach().clone().requires_grad_(p.training) if inp["bias"] is not None else None
+    h2d = sum(host[k].numel() * host[k].element_size() for k in ("input", "offset", "mask", "grad_output")
+              if host[k] is not None)
+    out_host = torch.empty(dev_w.shape, dtype=dev_w.dtype).pin_memory()
+    outb_host = torch.empty(dev_b.shape, dtype=dev_b.dtype).pin_memory() if dev_b is not None else None
+    d2h = out_host.numel() * out_host.element_size() + (outb_host.numel() * outb_host.element_size() if outb_host is not None else 0)
+
+    def one():
+        x = host["input"].to(dev, non_blocking=True).requires_grad_(p.training)
+        off = host["offset"].to(dev, non_blocking=True).requires_grad_(p.training)
+        m = host["mask"].to(dev, non_blocking=True).requires_grad_(p.training) if host["mask"] is not None else None
+        go = host["grad_output"].to(dev, non_blocking=True)
+        out = mdc.deform_conv2d(x, off, dev_w, dev_b, stride, pad, dil, m)
+        if p.training:
+            lv = [t for t in (x, off, dev_w, dev_b, m) if t is not None]
+            grads = torch.autograd.grad(out, lv, go)
+            gw = grads[2]
+            gb = grads[3] if dev_b is not None else None
+            if world > 1:
+                import torch.distributed as dist
+                flat = torch.cat([gw.reshape(-1)] + ([gb.reshape(-1)] if gb is not None else []))
+                dist.all_reduce(flat)
+                gw = flat[:gw.numel()].view_as(gw)
+                if gb is not None:
+                    gb = flat[gw.numel():]
+            out_host.copy_(gw, non_blocking=True)
+            if gb is not None:
+                outb_host.copy_(gb, non_blocking=True)
+        else:
+            out_host.copy_(dev_w, non_blocking=True)  # placeholder read of the same size
+    if not p.training:
+        o_host = torch.empty((inp["input"].shape[0], p.out_channels) + p.out_hw, dtype=p.dtype).pin_memory()
+        d2h = o_host.numel() * o_host.element_size()
+
+        def one():  # noqa: F811
+            x = host["input"].to(dev, non_blocking=True)
+            off = host["offset"].to(dev, non_blocking=True)
+            m = host["mask"].to(dev, non_blocking=True) if host["mask"] is not None else None
+            out = mdc.deform_conv2d(x, off, dev_w, dev_b, stride, pad, dil, m)
+            o_host.copy_(out, non_blocking=True)
+    for _ in range(max(args.warmup, 3)):
+        one()
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world)
+    tflops = p.flops(p.batch) * args.steps / (ms / 1e3) / 1e12
+    return {"value": round(tflops, 3), "unit": "TFLOP/s",
+            "samples_per_s": round(p.batch * args.steps / (ms / 1e3), 2),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+
+def cpu_baseline(p):
+    threads = os.cpu_count() or 1
+    nb = cpu_sample_batch(p)
+    inp = make_inputs(p, "cpu", batch=nb, dtype=torch.float32)
+    cpu_reference_step(p, inp, threads)  # warm-up
+    reps = 3
+    total = sum(cpu_reference_step(p, inp, threads) for _ in range(reps))
+    tflops = p.flops(nb) * reps / total / 1e12
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            "samples_per_s": round(nb * reps / total, 4),
+            "sample": f"{reps} x {nb} sample(s) of {p.name}, torchvision.ops.deform_conv2d CPU fp32 "
+                      f"fwd{'+bwd' if p.training else ''}, {threads} threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c5_train_bf16", choices=sorted(PROBLEMS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic-per-launch", type=float, default=None,
+                    help="ncu dram bytes per launch of the dominant kernel, if captured")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

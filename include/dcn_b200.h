@@ -1,0 +1,177 @@
+/*
+ * dcn_b200.h -- C ABI of the B200 (sm_100a) deformable-convolution library
+ * (libdcn_b200.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * a dense, row-major (NCHW) array of the element type named by desc->dtype,
+ * and every call is enqueued asynchronously on the CUDA stream passed as
+ * `stream` (a cudaStream_t; NULL = legacy default stream).  No call
+ * synchronises the host, and no call allocates device memory: scratch space
+ * is the caller's `workspace` (size from the *_workspace_size query, 256-byte
+ * aligned).  Inputs are never written.
+ *
+ * Each entry point replaces one function of the reference's native FFI (the
+ * pybind11 module `_C` of mps-deform-conv, mps_deform_conv/csrc/
+ * deform_conv2d_mps.mm:1221-1249), with the same argument meaning; the tensor
+ * arguments there become pointers plus the shape fields of dcn_conv_desc here.
+ *
+ * Layouts (B = batch, C = in_channels, G = n_weight_grps, OG = n_offset_grps,
+ * T = kernel_h * kernel_w, Ho/Wo = output size):
+ *   input       [B][C][H][W]
+ *   weight      [Co][C/G][kernel_h][kernel_w]
+ *   offset      [B][OG*T*2][Ho][Wo]   channel o*2T + 2t is dy, + 1 is dx
+ *   mask        [B][OG*T][Ho][Wo]     (ignored unless use_mask)
+ *   bias        [Co]                  (NULL = no bias)
+ *   output      [B][Co][Ho][Wo]
+ *   columns     [C*T][B*Ho*Wo]        row c*T + t
+ *
+ * Return value: DCN_OK or an error code; dcn_last_error() gives the message
+ * (thread-local).  Arithmetic: fp32 accumulation for every dtype.
+ */
+#ifndef DCN_B200_H
+#define DCN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DCN_API __attribute__((visibility("default")))
+#else
+#define DCN_API
+#endif
+
+/* element types (desc.dtype) */
+#define DCN_FLOAT32 0
+#define DCN_FLOAT16 1
+#define DCN_BFLOAT16 2
+
+/* status codes */
+#define DCN_OK 0
+#define DCN_ERR_INVALID_ARGUMENT 1 /* shape / parameter check failed          */
+#define DCN_ERR_UNSUPPORTED 2      /* dtype or size outside what is built     */
+#define DCN_ERR_CUDA 3             /* a CUDA runtime call or launch failed    */
+#define DCN_ERR_WORKSPACE 4        /* workspace pointer NULL or too small     */
+#define DCN_ERR_DEVICE_TIMEOUT 5   /* a kernel's bounded wait expired         */
+
+/* Problem descriptor: the integer arguments of the reference FFI
+ * (stride_h ... use_mask, deform_conv2d_mps.mm:603-615) plus the tensor
+ * shapes that the reference reads from its at::Tensor arguments. */
+typedef struct dcn_conv_desc {
+  int32_t dtype;          /* DCN_FLOAT32 / DCN_FLOAT16 / DCN_BFLOAT16 */
+  int32_t use_mask;       /* 0: DCNv1 (mask ignored), 1: DCNv2 */
+  int64_t batch, in_channels, in_h, in_w;
+  int64_t out_channels, kernel_h, kernel_w;
+  int64_t stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w;
+  int64_t n_weight_grps, n_offset_grps;
+} dcn_conv_desc;
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+DCN_API int dcn_abi_version(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads).  For launch accounting in benchmarks and tests. */
+DCN_API uint64_t dcn_launch_count(void);
+
+/* Per-kernel device timing.  While enabled, every launch this library makes
+ * is bracketed by a CUDA event pair recorded on its stream (launches inside a
+ * stream capture are not timed).  dcn_profile_enable(1) clears old records
+ * and starts; dcn_profile_enable(0) stops.  dcn_profile_summary waits for
+ * the recorded events and writes, per kernel name in order of first launch,
+ * the name (into names + i*name_stride), the launch count and the summed
+ * device time in ms; it returns the number of distinct names (-1 on a CUDA
+ * error) and writes at most max_entries entries. */
+DCN_API void dcn_profile_enable(int enable);
+DCN_API int dcn_profile_summary(int max_entries, char *names, size_t name_stride,
+                                uint64_t *launches, double *total_ms);
+
+/* Message of the last failed call on this host thread ("" if none). */
+DCN_API const char *dcn_last_error(void);
+
+/* Output spatial size for a descriptor; DCN_ERR_INVALID_ARGUMENT when it is
+ * not positive ("Invalid output dimensions", mps_deform_conv/__init__.py:208-216). */
+DCN_API int dcn_output_size(const dcn_conv_desc *desc, int64_t *out_h, int64_t *out_w);
+
+/* Checks a descriptor the way the reference's host code does
+ * (deform_conv2d_mps.mm:617-657: positive stride/dilation/groups,
+ * non-negative padding, int32 dispatch sizes) plus divisibility of the
+ * channel counts by the groups. */
+DCN_API int dcn_validate(const dcn_conv_desc *desc);
+
+/* ---------------------------------------------------------------------
+ * Forward.  Replaces `_C.deform_conv2d_forward` (deform_conv2d_mps.mm:603-800;
+ * argument-for-argument the torchvision::deform_conv2d schema):
+ * output = deformable conv of input with weight, offset, optional mask and
+ * bias.  Writes `output` completely.
+ */
+DCN_API size_t dcn_forward_workspace_size(const dcn_conv_desc *desc);
+DCN_API int dcn_deform_conv2d_forward(const dcn_conv_desc *desc, const void *input, const void *weight,
+                              const void *offset, const void *mask, const void *bias,
+                              void *output, void *workspace, size_t workspace_bytes,
+                              void *stream);
+
+/* ---------------------------------------------------------------------
+ * Column buffer.  Replaces `_C.deformable_im2col` (deform_conv2d_mps.mm:806-936):
+ * columns[c*T + t][b*Ho*Wo + p] = mask * bilinear(input[b, c], tap t at p).
+ * desc->out_channels, n_weight_grps are ignored.
+ */
+DCN_API int dcn_deformable_im2col(const dcn_conv_desc *desc, const void *input, const void *offset,
+                          const void *mask, void *columns, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Input gradient from a column gradient.  Replaces
+ * `_C.deform_conv2d_backward_input` (deform_conv2d_mps.mm:942-1069):
+ * grad_input = col2im(grad_col) (transpose of the bilinear gather, fp32
+ * accumulation).  grad_col has the columns layout.  Overwrites grad_input.
+ */
+DCN_API size_t dcn_backward_input_workspace_size(const dcn_conv_desc *desc);
+DCN_API int dcn_deform_conv2d_backward_input(const dcn_conv_desc *desc, const void *grad_col,
+                                     const void *offset, const void *mask, void *grad_input,
+                                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Offset and mask gradients from a column gradient.  Replaces
+ * `_C.deform_conv2d_backward_offset_mask` (deform_conv2d_mps.mm:1075-1215).
+ * Overwrites grad_offset, and grad_mask when use_mask (grad_mask may be
+ * NULL otherwise).
+ */
+DCN_API int dcn_deform_conv2d_backward_offset_mask(const dcn_conv_desc *desc, const void *grad_col,
+                                           const void *input, const void *offset,
+                                           const void *mask, void *grad_offset,
+                                           void *grad_mask, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Fused backward: all five gradients from grad_output in one call, with the
+ * grouped products done per group.  Replaces the reference's Python-side
+ * backward composition (mps_deform_conv/__init__.py:245-322: im2col
+ * recompute, two torch.mm GEMMs, backward_input, backward_offset_mask) --
+ * the schema of torchvision::_deform_conv2d_backward.  Any gradient pointer
+ * may be NULL to skip that gradient (grad_mask is only written when
+ * use_mask, grad_bias only when non-NULL).  Overwrites what it writes.
+ */
+DCN_API size_t dcn_backward_workspace_size(const dcn_conv_desc *desc);
+DCN_API int dcn_deform_conv2d_backward(const dcn_conv_desc *desc, const void *grad_output,
+                               const void *input, const void *weight, const void *offset,
+                               const void *mask, void *grad_input, void *grad_weight,
+                               void *grad_offset, void *grad_mask, void *grad_bias,
+                               void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Device status.  Kernels with bounded waits record an expired wait in a
+ * device-side status word instead of hanging.  This call copies and clears
+ * it (it synchronises `stream`): DCN_OK, or DCN_ERR_DEVICE_TIMEOUT.
+ */
+DCN_API int dcn_device_status(void *stream);
+
+/* Which implementation a descriptor runs on: 1 = tensor-core (tcgen05)
+ * kernels, 0 = general SIMT kernels (any shape, fp32 path). */
+DCN_API int dcn_uses_tensor_cores(const dcn_conv_desc *desc);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DCN_B200_H */

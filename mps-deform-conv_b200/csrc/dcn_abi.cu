@@ -1,0 +1,441 @@
+// dcn_abi.cu -- the extern "C" entry points declared in include/dcn_b200.h:
+// argument checks, workspace carving and dispatch to the kernel families
+// (tensor-core kernels where they apply, SIMT kernels otherwise).
+//
+// Error behaviour mirrors the reference host code
+// (mps_deform_conv/csrc/deform_conv2d_mps.mm:597-657): the same checks, the same
+// messages, reported through a status code and dcn_last_error() instead of a
+// C++ exception.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "dcn_internal.h"
+#include "dcn_tc.h"
+
+namespace dcn {
+
+static thread_local std::string g_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+// ---------------------------------------------------------------- profiling
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+static std::atomic<bool> g_prof_on{false};
+static std::mutex g_prof_mu;
+static std::vector<ProfRecord> g_prof;
+static std::vector<cudaEvent_t> g_event_pool;
+
+static cudaEvent_t prof_event() {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+KernelScope::KernelScope(const char* name, cudaStream_t st) : name_(name), st_(st) {
+  note_launch();
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+  start_ = prof_event();
+  if (start_ && cudaEventRecord(start_, st) != cudaSuccess) start_ = nullptr;
+}
+
+KernelScope::~KernelScope() {
+  if (!start_) return;
+  cudaEvent_t stop = prof_event();
+  if (!stop || cudaEventRecord(stop, st_) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof.push_back({name_, start_, stop});
+}
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* where) {
+  return fail(DCN_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)e, cudaGetErrorString(e));
+}
+
+static int ok() {
+  g_last_error.clear();
+  return DCN_OK;
+}
+
+// Output extent with floor division, as the reference's Python layer computes
+// it (mps_deform_conv/__init__.py:208-209): a padded input smaller than the
+// dilated kernel gives a non-positive extent and is rejected.
+static long long out_extent(long long in, long long pad, long long dil, long long k, long long stride) {
+  const long long num = in + 2 * pad - (dil * (k - 1) + 1);
+  const long long q = num >= 0 ? num / stride : -((-num + stride - 1) / stride);
+  return q + 1;
+}
+
+static size_t elem_size(int dtype) { return dtype == DCN_FLOAT32 ? 4 : 2; }
+
+static int validate(const dcn_conv_desc* d) {
+  if (!d) return fail(DCN_ERR_INVALID_ARGUMENT, "descriptor is NULL");
+  if (d->dtype != DCN_FLOAT32 && d->dtype != DCN_FLOAT16 && d->dtype != DCN_BFLOAT16)
+    return fail(DCN_ERR_UNSUPPORTED, "dtype %d is not one of float32, float16, bfloat16", d->dtype);
+  if (d->stride_h <= 0 || d->stride_w <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "stride must be positive, got stride=(%lld, %lld)",
+                (long long)d->stride_h, (long long)d->stride_w);
+  if (d->dilation_h <= 0 || d->dilation_w <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "dilation must be positive, got dilation=(%lld, %lld)",
+                (long long)d->dilation_h, (long long)d->dilation_w);
+  if (d->pad_h < 0 || d->pad_w < 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "padding must be non-negative, got padding=(%lld, %lld)",
+                (long long)d->pad_h, (long long)d->pad_w);
+  if (d->kernel_h <= 0 || d->kernel_w <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "kernel_size must be positive, got kernel=(%lld, %lld)",
+                (long long)d->kernel_h, (long long)d->kernel_w);
+  if (d->n_weight_grps <= 0) return fail(DCN_ERR_INVALID_ARGUMENT, "n_weight_grps must be positive");
+  if (d->n_offset_grps <= 0) return fail(DCN_ERR_INVALID_ARGUMENT, "n_offset_grps must be positive");
+  if (d->batch < 0 || d->in_channels <= 0 || d->in_h <= 0 || d->in_w <= 0 || d->out_channels <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT,
+                "tensor sizes must be positive (batch may be 0): batch=%lld in_channels=%lld "
+                "in_h=%lld in_w=%lld out_channels=%lld",
+                (long long)d->batch, (long long)d->in_channels, (long long)d->in_h,
+                (long long)d->in_w, (long long)d->out_channels);
+  if (d->in_channels % d->n_weight_grps != 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "in_channels (%lld) must be divisible by n_weight_grps (%lld)",
+                (long long)d->in_channels, (long long)d->n_weight_grps);
+  if (d->out_channels % d->n_weight_grps != 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "out_channels (%lld) must be divisible by n_weight_grps (%lld)",
+                (long long)d->out_channels, (long long)d->n_weight_grps);
+  if (d->in_channels % d->n_offset_grps != 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "in_channels (%lld) must be divisible by n_offset_grps (%lld)",
+                (long long)d->in_channels, (long long)d->n_offset_grps);
+  const long long out_h = out_extent(d->in_h, d->pad_h, d->dilation_h, d->kernel_h, d->stride_h);
+  const long long out_w = out_extent(d->in_w, d->pad_w, d->dilation_w, d->kernel_w, d->stride_w);
+  if (out_h <= 0 || out_w <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT,
+                "Invalid output dimensions: out_h=%lld, out_w=%lld. Check stride/padding/dilation values.",
+                out_h, out_w);
+  const long long lim = 2147483647LL;
+  const long long num_kernels = d->in_channels * out_h * out_w * d->batch;
+  if (num_kernels > lim)
+    return fail(DCN_ERR_UNSUPPORTED, "num_kernels (%lld) exceeds int32 limit. Reduce tensor dimensions.", num_kernels);
+  if (d->in_channels * d->kernel_h * d->kernel_w > lim)
+    return fail(DCN_ERR_UNSUPPORTED, "column_height (%lld) exceeds int32 limit. Reduce tensor dimensions.",
+                (long long)(d->in_channels * d->kernel_h * d->kernel_w));
+  if (d->batch * out_h * out_w > lim)
+    return fail(DCN_ERR_UNSUPPORTED, "column_width (%lld) exceeds int32 limit. Reduce tensor dimensions.",
+                (long long)(d->batch * out_h * out_w));
+  if (d->in_h * d->in_w > lim)
+    return fail(DCN_ERR_UNSUPPORTED, "in_h*in_w (%lld) exceeds int32 limit. Reduce tensor dimensions.",
+                (long long)(d->in_h * d->in_w));
+  if (d->out_channels * (d->in_channels / d->n_weight_grps) * d->kernel_h * d->kernel_w > lim)
+    return fail(DCN_ERR_UNSUPPORTED, "weight numel exceeds int32 limit");
+  return DCN_OK;
+}
+
+// Workspace layout of the fused backward on the SIMT kernels.
+struct SimtBwdLayout {
+  size_t gcol, gin32, gw32, goff, total;
+};
+static SimtBwdLayout simt_bwd_layout(const dcn_conv_desc* d, const Geom& g) {
+  SimtBwdLayout L;
+  const bool f32 = d->dtype == DCN_FLOAT32;
+  size_t off = 0;
+  L.gcol = off;  off += ws_align(sizeof(float) * (size_t)g.C * g.T * (size_t)g.P);
+  L.gin32 = off; off += f32 ? 0 : ws_align(sizeof(float) * (size_t)g.B * g.C * g.H * g.W);
+  L.gw32 = off;  off += f32 ? 0 : ws_align(sizeof(float) * (size_t)g.Co * g.Cig * g.T);
+  L.goff = off;  off += ws_align(elem_size(d->dtype) * (size_t)g.B * g.OG * 2 * g.T * g.HWo);
+  L.total = off;
+  return L;
+}
+
+template <typename F>
+static int dispatch_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case DCN_FLOAT32: return f((float*)nullptr);
+    case DCN_FLOAT16: return f((__half*)nullptr);
+    default: return f((__nv_bfloat16*)nullptr);
+  }
+}
+
+}  // namespace dcn
+
+using namespace dcn;
+
+extern "C" {
+
+int dcn_abi_version(void) { return 100; }
+
+uint64_t dcn_launch_count(void) { return (uint64_t)g_launches.load(std::memory_order_relaxed); }
+
+void dcn_profile_enable(int enable) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof) {
+    g_event_pool.push_back(r.start);
+    g_event_pool.push_back(r.stop);
+  }
+  g_prof.clear();
+  g_prof_on.store(enable != 0, std::memory_order_relaxed);
+}
+
+int dcn_profile_summary(int max_entries, char* names, size_t name_stride, uint64_t* launches,
+                        double* total_ms) {
+  std::vector<ProfRecord> recs;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    recs = g_prof;
+  }
+  std::vector<std::string> keys;
+  std::vector<uint64_t> cnt;
+  std::vector<double> ms;
+  for (auto& r : recs) {
+    if (cudaEventSynchronize(r.stop) != cudaSuccess) return -1;
+    float t = 0.f;
+    if (cudaEventElapsedTime(&t, r.start, r.stop) != cudaSuccess) return -1;
+    size_t i = 0;
+    while (i < keys.size() && keys[i] != r.name) ++i;
+    if (i == keys.size()) {
+      keys.push_back(r.name);
+      cnt.push_back(0);
+      ms.push_back(0.0);
+    }
+    cnt[i] += 1;
+    ms[i] += t;
+  }
+  const int n = (int)keys.size() < max_entries ? (int)keys.size() : max_entries;
+  for (int i = 0; i < n; ++i) {
+    if (names && name_stride) {
+      strncpy(names + (size_t)i * name_stride, keys[i].c_str(), name_stride - 1);
+      names[(size_t)i * name_stride + name_stride - 1] = 0;
+    }
+    if (launches) launches[i] = cnt[i];
+    if (total_ms) total_ms[i] = ms[i];
+  }
+  return (int)keys.size();
+}
+
+const char* dcn_last_error(void) { return g_last_error.c_str(); }
+
+int dcn_validate(const dcn_conv_desc* desc) {
+  int r = validate(desc);
+  return r == DCN_OK ? ok() : r;
+}
+
+int dcn_output_size(const dcn_conv_desc* d, int64_t* out_h, int64_t* out_w) {
+  if (!d || !out_h || !out_w) return fail(DCN_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (d->stride_h <= 0 || d->stride_w <= 0) return fail(DCN_ERR_INVALID_ARGUMENT, "stride must be positive");
+  *out_h = out_extent(d->in_h, d->pad_h, d->dilation_h, d->kernel_h, d->stride_h);
+  *out_w = out_extent(d->in_w, d->pad_w, d->dilation_w, d->kernel_w, d->stride_w);
+  if (*out_h <= 0 || *out_w <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT,
+                "Invalid output dimensions: out_h=%lld, out_w=%lld. Check stride/padding/dilation values.",
+                (long long)*out_h, (long long)*out_w);
+  return ok();
+}
+
+int dcn_uses_tensor_cores(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK) return 0;
+  return tc_supported(*d, make_geom(*d)) ? 1 : 0;
+}
+
+size_t dcn_forward_workspace_size(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK) return 0;
+  const Geom g = make_geom(*d);
+  return tc_supported(*d, g) ? tc_forward_workspace(*d, g) : 0;
+}
+
+int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const void* weight,
+                              const void* offset, const void* mask, const void* bias, void* output,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  int r = validate(d);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(*d);
+  if (g.P == 0) return ok();
+  if (!input || !weight || !offset || !output || (d->use_mask && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (input, weight, offset, output%s)",
+                d->use_mask ? ", mask" : "");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (tc_supported(*d, g)) {
+    const size_t need = tc_forward_workspace(*d, g);
+    if (workspace_bytes < need || (need && !workspace))
+      return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need,
+                  workspace_bytes);
+    cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward (tensor core)");
+  }
+  cudaError_t e = cudaSuccess;
+  dispatch_dtype(d->dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    e = simt_forward<T>(g, (const T*)input, (const T*)weight, (const T*)offset,
+                        (const T*)(d->use_mask ? mask : nullptr), (const T*)bias, (T*)output, st);
+    return 0;
+  });
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward");
+}
+
+int dcn_deformable_im2col(const dcn_conv_desc* d0, const void* input, const void* offset,
+                          const void* mask, void* columns, void* stream) {
+  dcn_conv_desc dd = *d0;
+  dd.out_channels = dd.n_weight_grps;  // unused by this call
+  int r = validate(&dd);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(dd);
+  if (g.P == 0) return ok();
+  if (!input || !offset || !columns || (dd.use_mask && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  cudaError_t e = cudaSuccess;
+  dispatch_dtype(dd.dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    e = simt_im2col<T>(g, (const T*)input, (const T*)offset, (const T*)(dd.use_mask ? mask : nullptr),
+                       (T*)columns, (cudaStream_t)stream);
+    return 0;
+  });
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deformable_im2col");
+}
+
+size_t dcn_backward_input_workspace_size(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK) return 0;
+  const Geom g = make_geom(*d);
+  return d->dtype == DCN_FLOAT32 ? 0 : ws_align(sizeof(float) * (size_t)g.B * g.C * g.H * g.W);
+}
+
+int dcn_deform_conv2d_backward_input(const dcn_conv_desc* d0, const void* grad_col,
+                                     const void* offset, const void* mask, void* grad_input,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  dcn_conv_desc dd = *d0;
+  dd.out_channels = dd.n_weight_grps;
+  int r = validate(&dd);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(dd);
+  cudaStream_t st = (cudaStream_t)stream;
+  const long long n = (long long)g.B * g.C * g.H * g.W;
+  if (n == 0) return ok();
+  if (!grad_col || !offset || !grad_input || (dd.use_mask && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  const size_t need = dcn_backward_input_workspace_size(&dd);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(DCN_ERR_WORKSPACE, "backward_input workspace too small: need %zu bytes, got %zu", need,
+                workspace_bytes);
+  cudaError_t e = cudaSuccess;
+  dispatch_dtype(dd.dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    float* acc = need ? (float*)workspace : (float*)grad_input;
+    if ((e = cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)n, st)) != cudaSuccess) return 0;
+    if ((e = simt_col2im<T, T>(g, (const T*)grad_col, (const T*)offset,
+                               (const T*)(dd.use_mask ? mask : nullptr), acc, st)) != cudaSuccess)
+      return 0;
+    if (need) e = convert_f32<T>(acc, (T*)grad_input, n, st);
+    return 0;
+  });
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_input");
+}
+
+int dcn_deform_conv2d_backward_offset_mask(const dcn_conv_desc* d0, const void* grad_col,
+                                           const void* input, const void* offset, const void* mask,
+                                           void* grad_offset, void* grad_mask, void* stream) {
+  dcn_conv_desc dd = *d0;
+  dd.out_channels = dd.n_weight_grps;
+  int r = validate(&dd);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(dd);
+  if (g.P == 0) return ok();
+  if (!grad_col || !input || !offset || !grad_offset || (dd.use_mask && (!mask || !grad_mask)))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  cudaError_t e = cudaSuccess;
+  dispatch_dtype(dd.dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    e = simt_col2im_coord<T, T>(g, (const T*)grad_col, (const T*)input, (const T*)offset,
+                                (const T*)(dd.use_mask ? mask : nullptr), (T*)grad_offset,
+                                (T*)(dd.use_mask ? grad_mask : nullptr), (cudaStream_t)stream);
+    return 0;
+  });
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_offset_mask");
+}
+
+size_t dcn_backward_workspace_size(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK) return 0;
+  const Geom g = make_geom(*d);
+  if (tc_supported(*d, g)) return tc_backward_workspace(*d, g);
+  return simt_bwd_layout(d, g).total;
+}
+
+int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, const void* input,
+                               const void* weight, const void* offset, const void* mask,
+                               void* grad_input, void* grad_weight, void* grad_offset,
+                               void* grad_mask, void* grad_bias, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  int r = validate(d);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(*d);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!d->use_mask) grad_mask = nullptr;
+  if (g.P == 0) {  // empty batch: parameter gradients are zero sums
+    cudaError_t e = cudaSuccess;
+    const size_t es = elem_size(d->dtype);
+    if (grad_weight) e = cudaMemsetAsync(grad_weight, 0, es * (size_t)g.Co * g.Cig * g.T, st);
+    if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, es * (size_t)g.Co, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
+  }
+  if (!grad_output || !input || !weight || !offset || (d->use_mask && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (grad_output, input, weight, offset%s)",
+                d->use_mask ? ", mask" : "");
+  if (tc_supported(*d, g)) {
+    const size_t need = tc_backward_workspace(*d, g);
+    if (workspace_bytes < need || (need && !workspace))
+      return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,
+                  workspace_bytes);
+    cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset, mask, grad_input, grad_weight,
+                                grad_offset, grad_mask, grad_bias, workspace, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward (tensor core)");
+  }
+  const SimtBwdLayout L = simt_bwd_layout(d, g);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", L.total,
+                workspace_bytes);
+  char* base = (char*)workspace;
+  const bool f32 = d->dtype == DCN_FLOAT32;
+  SimtBackwardWs ws;
+  ws.gcol = (float*)(base + L.gcol);
+  ws.gin32 = f32 ? nullptr : (float*)(base + L.gin32);
+  ws.gw32 = f32 ? nullptr : (float*)(base + L.gw32);
+  ws.goff_scratch = base + L.goff;
+  cudaError_t e = cudaSuccess;
+  dispatch_dtype(d->dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    e = simt_backward<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight,
+                         (const T*)offset, (const T*)(d->use_mask ? mask : nullptr), (T*)grad_input,
+                         (T*)grad_weight, (T*)grad_offset, (T*)grad_mask, (T*)grad_bias, ws, st);
+    return 0;
+  });
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
+}
+
+int dcn_device_status(void* stream) {
+  int v = 0;
+  cudaError_t e = tc_read_and_clear_status(&v, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "dcn_device_status");
+  if (v != 0) return fail(DCN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+// dcn_internal.h -- declarations shared by the kernel files and the C ABI layer.
+#pragma once
+
+#include "dcn_common.cuh"
+
+namespace dcn {
+
+// Scratch buffers of the SIMT backward (all fp32, caller-provided).
+struct SimtBackwardWs {
+  float* gcol;          // [C*T][P] column gradient
+  float* gin32;         // [B][C][H][W] fp32 grad_input accumulator (NULL when T is float)
+  float* gw32;          // [Co][C/G*T] fp32 grad_weight accumulator (NULL when T is float)
+  void* goff_scratch;   // offset-grad sink when the caller wants only grad_mask
+};
+
+template <typename T>
+cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
+                         const T* bias, T* out, cudaStream_t st);
+template <typename T>
+cudaError_t simt_im2col(const Geom& g, const T* x, const T* off, const T* msk, T* cols,
+                        cudaStream_t st);
+template <typename TC, typename T>
+cudaError_t simt_col2im(const Geom& g, const TC* gcol, const T* off, const T* msk, float* gin32,
+                        cudaStream_t st);
+template <typename TC, typename T>
+cudaError_t simt_col2im_coord(const Geom& g, const TC* gcol, const T* x, const T* off,
+                              const T* msk, T* goff, T* gmsk, cudaStream_t st);
+template <typename T>
+cudaError_t convert_f32(const float* src, T* dst, long long n, cudaStream_t st);
+template <typename T>
+cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, const T* off,
+                          const T* msk, T* gin, T* gw, T* goff, T* gmsk, T* gb,
+                          const SimtBackwardWs& ws, cudaStream_t st);
+
+// Counts kernel launches made by this library (dcn_launch_count()).
+void note_launch(int n = 1);
+
+// Scope around one kernel launch: counts it and, while profiling is enabled
+// (dcn_profile_enable), records a CUDA event pair on the launching stream so
+// the launch's device time can be read back per kernel name.
+class KernelScope {
+ public:
+  KernelScope(const char* name, cudaStream_t st);
+  ~KernelScope();
+  KernelScope(const KernelScope&) = delete;
+  KernelScope& operator=(const KernelScope&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t st_;
+  cudaEvent_t start_ = nullptr;
+};
+
+// Round a byte count up to the 256-byte workspace alignment.
+inline size_t ws_align(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace dcn

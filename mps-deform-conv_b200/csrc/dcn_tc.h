@@ -1,0 +1,25 @@
+// dcn_tc.h -- tensor-core (tcgen05 / TMEM) kernel family: which problems it
+// takes, how much workspace it needs, and its launchers.
+#pragma once
+
+#include "dcn_internal.h"
+
+namespace dcn {
+
+// True when the tensor-core kernels handle this problem (fp16/bf16 and the
+// channel/size constraints listed in dcn_tc.cu).
+bool tc_supported(const dcn_conv_desc& d, const Geom& g);
+size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g);
+size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g);
+cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
+                       const void* offset, const void* mask, const void* bias, void* output,
+                       void* workspace, cudaStream_t st);
+cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output,
+                        const void* input, const void* weight, const void* offset, const void* mask,
+                        void* grad_input, void* grad_weight, void* grad_offset, void* grad_mask,
+                        void* grad_bias, void* workspace, cudaStream_t st);
+// Copies the device status word (non-zero after an expired bounded wait)
+// into *out and clears it; synchronises the stream.
+cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st);
+
+}  // namespace dcn

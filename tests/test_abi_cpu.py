@@ -1,0 +1,102 @@
+"""The C ABI library loads, exports every declared symbol, and its host-side
+checks behave like the reference's (no GPU needed: nothing here launches)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "dcn_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"DCN_API\s+[\w\s\*]+?\b(dcn_\w+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    names = declared_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), f"libdcn_b200.so does not export {n}"
+    # and the ctypes binding declares exactly the header's surface
+    assert set(_abi.SIGNATURES) == set(names)
+
+
+def test_abi_version():
+    from mps_deform_conv import _abi
+    assert _abi.load().dcn_abi_version() >= 100
+
+
+def _desc(**kw):
+    from mps_deform_conv import _abi
+    base = dict(dtype=_abi.DCN_FLOAT32, input_shape=(1, 4, 8, 8), weight_shape=(4, 4, 3, 3))
+    base.update(kw)
+    return _abi.make_desc(base.pop("dtype"), base.pop("input_shape"), base.pop("weight_shape"), **base)
+
+
+@pytest.mark.parametrize("kw,needle", [
+    (dict(stride=(0, 1)), "stride must be positive"),
+    (dict(dilation=(1, 0)), "dilation must be positive"),
+    (dict(padding=(-1, 0)), "padding must be non-negative"),
+    (dict(n_weight_grps=3), "divisible"),
+    (dict(n_offset_grps=3), "divisible"),
+    (dict(input_shape=(1, 4, 4, 4), weight_shape=(4, 4, 5, 5), stride=(2, 2)), "Invalid output dimensions"),
+    (dict(dtype=7), "dtype"),
+    (dict(input_shape=(70000, 512, 64, 64)), "exceeds int32 limit"),
+])
+def test_validate_messages(kw, needle):
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    d = _desc(**kw)
+    rc = lib.dcn_validate(ctypes.byref(d))
+    assert rc != _abi.DCN_OK
+    assert needle in lib.dcn_last_error().decode()
+
+
+def test_validate_ok_and_output_size():
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    d = _desc(padding=(1, 1))
+    assert lib.dcn_validate(ctypes.byref(d)) == _abi.DCN_OK
+    assert _abi.output_size(d) == (8, 8)
+    d = _desc(stride=(2, 2), dilation=(2, 2), padding=(2, 2), input_shape=(1, 4, 9, 8))
+    assert _abi.output_size(d) == (5, 4)
+
+
+def test_workspace_sizes_are_host_queries():
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    d = _desc(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3),
+              padding=(1, 1), use_mask=True)
+    assert lib.dcn_backward_workspace_size(ctypes.byref(d)) > 0
+    assert lib.dcn_backward_input_workspace_size(ctypes.byref(d)) == 2 * 64 * 16 * 16 * 4
+    bad = _desc(stride=(0, 0))
+    assert lib.dcn_backward_workspace_size(ctypes.byref(bad)) == 0
+
+
+def test_forward_rejects_null_and_small_workspace_without_launching():
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    d = _desc(padding=(1, 1))
+    rc = lib.dcn_deform_conv2d_forward(ctypes.byref(d), None, None, None, None, None, None, None, 0, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT
+    assert "NULL" in lib.dcn_last_error().decode()
+    bd = _desc(padding=(1, 1))
+    rc = lib.dcn_deform_conv2d_backward(ctypes.byref(bd), ctypes.c_void_p(16), ctypes.c_void_p(16),
+                                        ctypes.c_void_p(16), ctypes.c_void_p(16), None, None, None,
+                                        None, None, None, None, 0, None)
+    assert rc == _abi.DCN_ERR_WORKSPACE
+
+
+def test_torch_extension_imports():
+    import mps_deform_conv
+    lib = mps_deform_conv._get_lib()
+    for f in ("deform_conv2d_forward", "deformable_im2col", "deform_conv2d_backward_input",
+              "deform_conv2d_backward_offset_mask", "deform_conv2d_backward"):
+        assert hasattr(lib, f)
+    assert lib.abi_version() >= 100

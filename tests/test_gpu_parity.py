@@ -1,0 +1,134 @@
+"""GPU parity: the CUDA kernels against the float64 oracle and the torchvision
+golden fixtures, for every dtype, through the C ABI (ctypes, libdcn_b200.so)
+and through the Python API (mps_deform_conv, autograd).
+
+Tolerance: normwise relative error (tests/_util.rel_err) <= 1e-4 for fp32 and
+<= 1e-2 for fp16/bf16, per output and per gradient.  For fp16/bf16 the oracle
+runs on the same rounded inputs the GPU sees.
+"""
+import numpy as np
+import pytest
+import torch
+
+from _util import TOL, golden_cases, load_golden, rel_err, to_np
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+CASES = [c for c in golden_cases() if c != "empty_batch"]
+
+
+def _tensors(d, dtype, dev):
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype)
+    return dict(input=t(d["input"]), offset=t(d["offset"]), weight=t(d["weight"]),
+                bias=t(d.get("bias")), mask=t(d.get("mask")), grad_output=t(d["grad_output"]))
+
+
+def _geo(d):
+    return tuple(int(v) for v in d["stride"]), tuple(int(v) for v in d["padding"]), \
+        tuple(int(v) for v in d["dilation"])
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+@pytest.mark.parametrize("name", CASES)
+def test_abi_forward_backward_vs_oracle(name, dtype, cuda):
+    from mps_deform_conv import _abi
+    d = load_golden(name)
+    st, pd, dl = _geo(d)
+    T = _tensors(d, DTYPES[dtype], cuda)
+    out = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    gi, goff, gw, gb, gm = _abi.call_backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                              st, pd, dl, T["mask"], with_bias=T["bias"] is not None)
+    torch.cuda.synchronize()
+    # oracle on exactly the values the GPU saw
+    ref_out = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                                st, pd, dl, T["mask"], T["bias"] is not None)
+    tol = TOL[dtype]
+    assert rel_err(to_np(out), ref_out) <= tol
+    assert rel_err(to_np(gi), rgi) <= tol
+    assert rel_err(to_np(goff), rgoff) <= tol
+    assert rel_err(to_np(gw), rgw) <= tol
+    if T["bias"] is not None:
+        assert rel_err(to_np(gb), rgb) <= tol
+    if T["mask"] is not None:
+        assert rel_err(to_np(gm), rgm) <= tol
+    if dtype == "float32":  # and directly against the torchvision fixtures
+        assert rel_err(to_np(out), d["output"]) <= tol
+        assert rel_err(to_np(gi), d["grad_input"]) <= tol
+        assert rel_err(to_np(goff), d["grad_offset"]) <= tol
+        assert rel_err(to_np(gw), d["grad_weight"]) <= tol
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+@pytest.mark.parametrize("name", ["mask_bias_g2_og2", "stride2_dil2", "basic_v1", "far_offsets_og4"])
+def test_python_api_autograd_vs_oracle(name, dtype, cuda):
+    import mps_deform_conv as mdc
+    d = load_golden(name)
+    st, pd, dl = _geo(d)
+    T = _tensors(d, DTYPES[dtype], cuda)
+    leaves = {k: T[k].clone().requires_grad_(True) for k in ("input", "offset", "weight", "bias", "mask")
+              if T[k] is not None}
+    out = mdc.deform_conv2d(leaves["input"], leaves["offset"], leaves["weight"], leaves.get("bias"),
+                            st, pd, dl, leaves.get("mask"))
+    out.backward(T["grad_output"])
+    ref_out = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                                st, pd, dl, T["mask"], T["bias"] is not None)
+    tol = TOL[dtype]
+    assert out.dtype == DTYPES[dtype] and out.is_cuda
+    assert rel_err(to_np(out), ref_out) <= tol
+    assert rel_err(to_np(leaves["input"].grad), rgi) <= tol
+    assert rel_err(to_np(leaves["offset"].grad), rgoff) <= tol
+    assert rel_err(to_np(leaves["weight"].grad), rgw) <= tol
+    if "bias" in leaves:
+        assert rel_err(to_np(leaves["bias"].grad), rgb) <= tol
+    if "mask" in leaves:
+        assert rel_err(to_np(leaves["mask"].grad), rgm) <= tol
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+def test_reference_column_interface(dtype, cuda):
+    """The reference FFI's column-buffer functions: deformable_im2col,
+    deform_conv2d_backward_input, deform_conv2d_backward_offset_mask."""
+    import mps_deform_conv as mdc
+    lib = mdc._get_lib()
+    d = load_golden("mask_bias_g2_og2")
+    st, pd, dl = _geo(d)
+    T = _tensors(d, DTYPES[dtype], cuda)
+    kh, kw = T["weight"].shape[2:]
+    og = T["offset"].shape[1] // (2 * kh * kw)
+    x, off, m = T["input"], T["offset"], T["mask"]
+    cols = lib.deformable_im2col(x, off, m, kh, kw, st[0], st[1], pd[0], pd[1], dl[0], dl[1], og, True)
+    rcols = oracle.im2col(x, off, m, kh, kw, st, pd, dl, og)
+    assert tuple(cols.shape) == rcols.shape
+    assert rel_err(to_np(cols), rcols) <= TOL[dtype]
+    gcol = torch.randn(cols.shape, device=cuda, dtype=torch.float32).to(DTYPES[dtype])
+    gi = lib.deform_conv2d_backward_input(gcol, x, off, m, x.shape[2], x.shape[3], st[0], st[1], pd[0],
+                                          pd[1], dl[0], dl[1], kh, kw, og, True)
+    rgi = oracle.col2im(gcol, tuple(x.shape), off, m, kh, kw, st, pd, dl, og)
+    assert rel_err(to_np(gi), rgi) <= TOL[dtype]
+    goff, gm = lib.deform_conv2d_backward_offset_mask(gcol, x, off, m, kh, kw, st[0], st[1], pd[0],
+                                                      pd[1], dl[0], dl[1], og, True)
+    rgoff, rgm = oracle.col2im_coord(gcol, x, off, m, kh, kw, st, pd, dl, og)
+    assert rel_err(to_np(goff), rgoff) <= TOL[dtype]
+    assert rel_err(to_np(gm), rgm) <= TOL[dtype]
+
+
+def test_empty_batch(cuda):
+    import mps_deform_conv as mdc
+    d = load_golden("empty_batch")
+    st, pd, dl = _geo(d)
+    T = _tensors(d, torch.float32, cuda)
+    w = T["weight"].clone().requires_grad_(True)
+    b = T["bias"].clone().requires_grad_(True)
+    out = mdc.deform_conv2d(T["input"], T["offset"], w, b, st, pd, dl, T["mask"])
+    assert tuple(out.shape) == d["output"].shape
+    out.sum().backward()
+    assert torch.count_nonzero(w.grad) == 0 and torch.count_nonzero(b.grad) == 0
+
+
+def test_device_status_clean_after_runs(cuda):
+    import mps_deform_conv as mdc
+    mdc._get_lib().device_status()
