@@ -190,11 +190,13 @@ uint64_t dcn_launch_count(void) { return (uint64_t)g_launches.load(std::memory_o
 
 void dcn_profile_enable(int enable) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
-  for (auto& r : g_prof) {
-    g_event_pool.push_back(r.start);
-    g_event_pool.push_back(r.stop);
+  if (enable) {  // a new recording starts: recycle the previous one's events
+    for (auto& r : g_prof) {
+      g_event_pool.push_back(r.start);
+      g_event_pool.push_back(r.stop);
+    }
+    g_prof.clear();
   }
-  g_prof.clear();
   g_prof_on.store(enable != 0, std::memory_order_relaxed);
 }
 
