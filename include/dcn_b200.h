@@ -133,6 +133,28 @@ DCN_API int dcn_deform_conv2d_backward_input(const dcn_conv_desc *desc, const vo
                                      void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------
+ * Input gradient from a column gradient, allocating nothing.  No counterpart
+ * in the reference: it exists for callers that hold only their input and
+ * output buffers and cannot allocate device memory (plugin interfaces that
+ * hand a kernel library pointers but no allocator; real-time loops that
+ * forbid allocation after start-up).  Same arguments and result as
+ * dcn_deform_conv2d_backward_input, without the workspace: the fp32
+ * accumulator for fp16/bf16 data is a fixed 8 MiB array in device memory
+ * that every GPU which loads the library holds until the process exits.
+ *   - Limit: grad_input (B*C*H*W) may have at most 2,097,152 elements;
+ *     larger problems return DCN_ERR_UNSUPPORTED.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array and each call clears the part it uses.
+ *     Calls that overlap on the GPU (other streams, other host threads, same
+ *     device) race on it: issue them on one stream.
+ */
+DCN_API int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc *desc, const void *grad_col,
+                                                     const void *offset, const void *mask,
+                                                     void *grad_input, void *stream);
+
+/* ---------------------------------------------------------------------
  * Offset and mask gradients from a column gradient.  Replaces
  * `_C.deform_conv2d_backward_offset_mask` (deform_conv2d_mps.mm:1075-1215).
  * Overwrites grad_offset, and grad_mask when use_mask (grad_mask may be

@@ -432,6 +432,30 @@ int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, 
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
 }
 
+int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void* grad_col,
+                                             const void* offset, const void* mask,
+                                             void* grad_input, void* stream) {
+  dcn_conv_desc dd = *d0;
+  dd.out_channels = dd.n_weight_grps;
+  int r = validate(&dd);
+  if (r != DCN_OK) return r;
+  const Geom g = make_geom(dd);
+  const long long n = (long long)g.B * g.C * g.H * g.W;
+  if (n > noalloc_max_elems())
+    return fail(DCN_ERR_UNSUPPORTED,
+                "backward_input_noalloc: grad_input has %lld elements, more than the %lld this "
+                "allocation-free entry point supports; use dcn_deform_conv2d_backward_input with a "
+                "workspace",
+                n, noalloc_max_elems());
+  if (n == 0) return ok();
+  if (!grad_col || !offset || !grad_input || (dd.use_mask && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  cudaError_t e = noalloc_backward_input_dispatch(dd.dtype, g, grad_col, offset,
+                                                  dd.use_mask ? mask : nullptr, grad_input,
+                                                  (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_input_noalloc");
+}
+
 int dcn_device_status(void* stream) {
   int v = 0;
   cudaError_t e = tc_read_and_clear_status(&v, (cudaStream_t)stream);

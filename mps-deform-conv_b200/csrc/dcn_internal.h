@@ -32,6 +32,13 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
                           const T* msk, T* gin, T* gw, T* goff, T* gmsk, T* gb,
                           const SimtBackwardWs& ws, cudaStream_t st);
 
+// Allocation-free input gradient (dcn_noalloc.cu): largest grad_input it
+// accepts, and the launcher that uses the library's fixed device array.
+long long noalloc_max_elems();
+cudaError_t noalloc_backward_input_dispatch(int dtype, const Geom& g, const void* gcol,
+                                            const void* off, const void* msk, void* gin,
+                                            cudaStream_t st);
+
 // Counts kernel launches made by this library (dcn_launch_count()).
 void note_launch(int n = 1);
 

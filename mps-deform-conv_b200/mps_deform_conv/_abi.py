@@ -54,6 +54,7 @@ SIGNATURES = {
     "dcn_deformable_im2col": (ctypes.c_int, [_D, _V, _V, _V, _V, _V]),
     "dcn_backward_input_workspace_size": (_SZ, [_D]),
     "dcn_deform_conv2d_backward_input": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _SZ, _V]),
+    "dcn_deform_conv2d_backward_input_noalloc": (ctypes.c_int, [_D, _V, _V, _V, _V, _V]),
     "dcn_deform_conv2d_backward_offset_mask": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V]),
     "dcn_backward_workspace_size": (_SZ, [_D]),
     "dcn_deform_conv2d_backward": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
