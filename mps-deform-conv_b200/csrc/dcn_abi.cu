@@ -257,13 +257,13 @@ int dcn_output_size(const dcn_conv_desc* d, int64_t* out_h, int64_t* out_w) {
 
 int dcn_uses_tensor_cores(const dcn_conv_desc* d) {
   if (validate(d) != DCN_OK) return 0;
-  return tc_supported(*d, make_geom(*d)) ? 1 : 0;
+  return tc_forward_supported(*d, make_geom(*d)) ? 1 : 0;
 }
 
 size_t dcn_forward_workspace_size(const dcn_conv_desc* d) {
   if (validate(d) != DCN_OK) return 0;
   const Geom g = make_geom(*d);
-  return tc_supported(*d, g) ? tc_forward_workspace(*d, g) : 0;
+  return tc_forward_supported(*d, g) ? tc_forward_workspace(*d, g) : 0;
 }
 
 int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const void* weight,
@@ -277,7 +277,7 @@ int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const v
     return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (input, weight, offset, output%s)",
                 d->use_mask ? ", mask" : "");
   cudaStream_t st = (cudaStream_t)stream;
-  if (tc_supported(*d, g)) {
+  if (tc_forward_supported(*d, g)) {
     const size_t need = tc_forward_workspace(*d, g);
     if (workspace_bytes < need || (need && !workspace))
       return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need,
@@ -377,7 +377,7 @@ int dcn_deform_conv2d_backward_offset_mask(const dcn_conv_desc* d0, const void* 
 size_t dcn_backward_workspace_size(const dcn_conv_desc* d) {
   if (validate(d) != DCN_OK) return 0;
   const Geom g = make_geom(*d);
-  if (tc_supported(*d, g)) return tc_backward_workspace(*d, g);
+  if (tc_backward_supported(*d, g)) return tc_backward_workspace(*d, g);
   return simt_bwd_layout(d, g).total;
 }
 
@@ -401,7 +401,7 @@ int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, 
   if (!grad_output || !input || !weight || !offset || (d->use_mask && !mask))
     return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (grad_output, input, weight, offset%s)",
                 d->use_mask ? ", mask" : "");
-  if (tc_supported(*d, g)) {
+  if (tc_backward_supported(*d, g)) {
     const size_t need = tc_backward_workspace(*d, g);
     if (workspace_bytes < need || (need && !workspace))
       return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,

@@ -1,18 +1,486 @@
 // dcn_tc.cu -- tensor-core (tcgen05 / TMEM) kernels for sm_100a.
+//
+// Forward (dcn_fwd_tc_kernel): an implicit GEMM
+//     out[p][co] = sum_k A[p][k] * W[co][k] (+ bias[co])
+// over M = 128 output pixels per CTA, N = C_out of one weight group, and
+// K = (channel chunk of 64, tap) -- the reference's deformable_im2col
+// (deform_conv2d_mps.mm:105-340) fused as the producer of the A operand and its
+// at::mm / at::bmm (mm:765-782) as the tcgen05 MMA, so the column buffer never
+// exists in memory.
+//
+// Warp roles (320 threads):
+//   warps 0-7  gather producers: each thread owns one pixel row of the A tile
+//              and half of its 64 channels; it reads the offset/mask of its
+//              (pixel, tap, offset group), loads the 4 bilinear corners as
+//              16-byte channel vectors from the channels-last copy of the
+//              input, blends them in fp32 and writes the 128-byte-swizzled A
+//              row to shared memory.  After the main loop the same warps are
+//              the epilogue: TMEM -> registers -> +bias -> NCHW store.
+//   warp 8     MMA issuer (one thread) and TMEM owner.
+//   warp 9     weight loader: one bulk copy (TMA engine) per K chunk of the
+//              pre-swizzled weight image; no multicast.
+// Every mbarrier wait is bounded (dcn_sm100.cuh): on expiry the kernel sets
+// the device status word and unwinds.
+#include <type_traits>
+
+#include "dcn_sm100.cuh"
 #include "dcn_tc.h"
 
 namespace dcn {
 
+using namespace sm100;
+
+namespace sm100 {
 // Device status word: set by a kernel whose bounded wait expired.
 __device__ int g_dcn_status = 0;
+}  // namespace sm100
 
-bool tc_supported(const dcn_conv_desc&, const Geom&) { return false; }
-size_t tc_forward_workspace(const dcn_conv_desc&, const Geom&) { return 0; }
-size_t tc_backward_workspace(const dcn_conv_desc&, const Geom&) { return 0; }
-cudaError_t tc_forward(const dcn_conv_desc&, const Geom&, const void*, const void*, const void*,
-                       const void*, const void*, void*, void*, cudaStream_t) {
-  return cudaErrorNotSupported;
+namespace {
+
+constexpr int BM = 128;           // pixels per tile (MMA M)
+constexpr int BK = 64;            // channels per K chunk (one 128-byte row)
+constexpr int NPROD_WARPS = 8;
+constexpr int NPROD = NPROD_WARPS * 32;
+constexpr int MMA_WARP = 8;
+constexpr int LOAD_WARP = 9;
+constexpr int NTHREADS = 320;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+
+// status codes recorded on a wait that expired
+constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16;
+
+template <typename T> struct Vec;
+template <> struct Vec<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Vec<__half> {
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    return __half22float2(h);
+  }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+struct FwdSmem {  // offsets within the 1024-aligned dynamic shared memory
+  uint32_t a, b, bar, total;
+  int stages;
+  uint32_t b_stage_bytes;
+};
+
+__host__ __device__ inline FwdSmem fwd_smem_layout(int Cog, int stages) {
+  FwdSmem L;
+  L.stages = stages;
+  L.b_stage_bytes = (uint32_t)Cog * 128u;
+  L.a = 0;
+  L.b = L.a + stages * A_STAGE_BYTES;
+  L.bar = L.b + stages * L.b_stage_bytes;
+  // a_full[S], b_full[S], empty[S], acc_full, drain (8 B each) + tmem slot + abort flag
+  L.total = L.bar + (3 * stages + 2) * 8 + 16;
+  return L;
 }
+
+struct FwdArgs {
+  const void* xh;     // input, channels-last [B][H][W][C]
+  const void* off;    // offset NCHW
+  const void* msk;    // mask NCHW or null
+  const void* bias;   // [Co] or null
+  void* out;          // [B][Co][Ho][Wo]
+  const void* wsw;    // weights, pre-swizzled [G][NKC][Cog][64]
+  int* status;
+  Geom g;
+  int nkc;            // K chunks per group = (Cig / 64) * T
+  int stages;
+  int n_mma;          // MMAs per K step along N (Cog / n_mma <= 256)
+  uint32_t idesc;     // instruction descriptor for N = Cog / n_mma
+  uint32_t tmem_cols;
+};
+
+// ---------------------------------------------------------------- producer
+// Gathers one K chunk (tap t, 64 channels starting at c_abs0) of pixel row r
+// for this thread's 4 channel vectors [v0, v0+4) into the swizzled A row.
+template <typename T>
+__device__ __forceinline__ void gather_row(const FwdArgs& a, const T* __restrict__ xh,
+                                           const T* __restrict__ off, const T* __restrict__ msk,
+                                           uint8_t* arow, int r, int v0, bool valid, int b, int p,
+                                           int t, int c_abs0) {
+  const Geom& g = a.g;
+  uint4 vals[4][4];
+  float wts[4][4];
+  int cur_o = -1;
+  float w4[4] = {0.f, 0.f, 0.f, 0.f};
+  long long base4[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const int c_abs = c_abs0 + (v0 + v) * 8;
+    if (valid) {
+      const int o = c_abs / g.cpo;
+      if (o != cur_o) {
+        cur_o = o;
+        float y, x, m;
+        sample_point(g, off, msk, b, o, t, p, &y, &x, &m);
+        const Corners cs = corners_of(y, x, g.H, g.W);
+        const long long img = (long long)b * g.H * g.W;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          w4[k] = cs.w[k] * m;
+          base4[k] = (img + cs.idx[k]) * g.C;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        wts[v][k] = w4[k];
+        vals[v][k] = (w4[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(xh + base4[k] + c_abs))
+                                    : make_uint4(0, 0, 0, 0);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        wts[v][k] = 0.f;
+        vals[v][k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&vals[v][0]);
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&vals[v][1]);
+    const uint32_t* q2 = reinterpret_cast<const uint32_t*>(&vals[v][2]);
+    const uint32_t* q3 = reinterpret_cast<const uint32_t*>(&vals[v][3]);
+    uint32_t o4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f0 = Vec<T>::unpack(q0[e]), f1 = Vec<T>::unpack(q1[e]);
+      const float2 f2 = Vec<T>::unpack(q2[e]), f3 = Vec<T>::unpack(q3[e]);
+      const float lo = wts[v][0] * f0.x + wts[v][1] * f1.x + wts[v][2] * f2.x + wts[v][3] * f3.x;
+      const float hi = wts[v][0] * f0.y + wts[v][1] * f1.y + wts[v][2] * f2.y + wts[v][3] * f3.y;
+      o4[e] = Vec<T>::pack(lo, hi);
+    }
+    const int chunk = v0 + v;
+    uint4* dst = reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4));
+    *dst = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Geom& g = a.g;
+  const int S = a.stages;
+  const FwdSmem L = fwd_smem_layout(g.Cog, S);
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar_base = sbase + L.bar;
+  auto a_full = [&](int s) { return bar_base + 8u * s; };
+  auto b_full = [&](int s) { return bar_base + 8u * (S + s); };
+  auto empty = [&](int s) { return bar_base + 8u * (2 * S + s); };
+  const uint32_t acc_full = bar_base + 8u * (3 * S);
+  const uint32_t drain = bar_base + 8u * (3 * S + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (3 * S + 2) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.bar + (3 * S + 2) * 8 + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, grp = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(a_full(s), NPROD);
+      mbar_init(b_full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(smem_addr(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const T* xh = static_cast<const T*>(a.xh);
+  const T* off = static_cast<const T*>(a.off);
+  const T* msk = static_cast<const T*>(a.msk);
+
+  if (warp < NPROD_WARPS) {
+    // ------------------------------------------------ producers
+    const int r = threadIdx.x & (BM - 1);
+    const int v0 = (threadIdx.x >> 7) * 4;
+    const long long pix = (long long)tile * BM + r;
+    const bool valid = pix < g.P;
+    const int b = valid ? (int)(pix / g.HWo) : 0;
+    const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
+    bool ok = true;
+    for (int i = 0; i < a.nkc && ok; ++i) {
+      const int s = i % S;
+      const uint32_t parity = ((i / S) & 1) ^ 1;
+      ok = mbar_wait(empty(s), parity, abort_flag, a.status, ST_PROD);
+      if (!ok) break;
+      const int t = i % g.T, cc = i / g.T;
+      gather_row<T>(a, xh, off, msk, smem + L.a + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
+                    t, grp * g.Cig + cc * BK);
+      fence_async_shared();
+      mbar_arrive(a_full(s));
+    }
+    // ------------------------------------------------ epilogue
+    // (warp-uniform decision: tcgen05.ld is a .sync.aligned warp instruction)
+    const bool acc_ready = ok && mbar_wait(acc_full, 0, abort_flag, a.status, ST_EPI);
+    if (__all_sync(0xffffffffu, acc_ready)) {
+      tc_fence_after();
+      const int q = warp & 3, half = warp >> 2;
+      const int ncol = g.Cog / 2;
+      const int row = q * 32 + lane;
+      const long long opix = (long long)tile * BM + row;
+      const bool ovalid = opix < g.P;
+      const int ob = ovalid ? (int)(opix / g.HWo) : 0;
+      const int op = ovalid ? (int)(opix - (long long)ob * g.HWo) : 0;
+      T* out = static_cast<T*>(a.out);
+      const T* bias = static_cast<const T*>(a.bias);
+      for (int c0 = half * ncol; c0 < (half + 1) * ncol; c0 += 16) {
+        uint32_t acc[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, acc);
+        tmem_ld_wait();
+        if (ovalid) {
+          const int oc0 = grp * g.Cog + c0;
+          T* dst = out + ((long long)ob * g.Co + oc0) * g.HWo + op;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = __uint_as_float(acc[j]);
+            if (bias) v += to_f(bias[oc0 + j]);
+            dst[(long long)j * g.HWo] = from_f<T>(v);
+          }
+        }
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int nsub = g.Cog / a.n_mma;
+      bool ok = true;
+      int issued = 0;
+      for (int i = 0; i < a.nkc && ok; ++i) {
+        const int s = i % S;
+        const uint32_t parity = (i / S) & 1;
+        ok = mbar_wait(a_full(s), parity, abort_flag, a.status, ST_MMA_A) &&
+             mbar_wait(b_full(s), parity, abort_flag, a.status, ST_MMA_B);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t as = sbase + L.a + s * A_STAGE_BYTES;
+        const uint32_t bs = sbase + L.b + s * L.b_stage_bytes;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = desc_kmajor_sw128(as + k * 32);
+          for (int n = 0; n < a.n_mma; ++n) {
+            const uint64_t bd = desc_kmajor_sw128(bs + n * nsub * 128 + k * 32);
+            mma_f16(tmem + (uint32_t)(n * nsub), ad, bd, a.idesc, (i > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(empty(s));
+        ++issued;
+      }
+      if (ok) {
+        mma_commit(acc_full);
+      } else if (issued > 0) {
+        // let the MMAs already issued finish before TMEM is released
+        mma_commit(drain);
+        mbar_wait(drain, 0, abort_flag, a.status, ST_DRAIN);
+      }
+    }
+  } else {
+    // ------------------------------------------------ weight loader
+    if (lane == 0) {
+      const uint8_t* wbase = static_cast<const uint8_t*>(a.wsw) +
+                             (size_t)grp * a.nkc * L.b_stage_bytes;
+      int issued = 0;
+      for (int i = 0; i < a.nkc; ++i) {
+        const int s = i % S;
+        const uint32_t parity = ((i / S) & 1) ^ 1;
+        if (!mbar_wait(empty(s), parity, abort_flag, a.status, ST_LOAD)) break;
+        mbar_arrive_expect_tx(b_full(s), L.b_stage_bytes);
+        bulk_g2s(sbase + L.b + s * L.b_stage_bytes, wbase + (size_t)i * L.b_stage_bytes,
+                 L.b_stage_bytes, b_full(s));
+        ++issued;
+      }
+      // copies still in flight must land before the CTA exits
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+        mbar_wait(b_full(i % S), (i / S) & 1, abort_flag, a.status, ST_LOAD);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------- repacks
+// input NCHW -> channels-last [B][H][W][C], 64x64 tiles through shared memory.
+template <typename T>
+__global__ void nchw_to_nhwc_kernel(const T* __restrict__ x, T* __restrict__ xh, int C, int HW) {
+  __shared__ T tile[64][65];
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.y * 64, hw0 = blockIdx.x * 64;
+  const T* src = x + (long long)b * C * HW;
+  T* dst = xh + (long long)b * C * HW;
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int cc = e / 64, hh = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) tile[cc][hh] = src[(long long)c * HW + hw];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int hh = e / 64, cc = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) dst[(long long)hw * C + c] = tile[cc][hh];
+  }
+}
+
+// weight [Co][Cig][T] -> [G][NKC][Cog][64], K chunk kc = (cc, t) with t
+// fastest, rows 128-byte swizzled (chunk j of row co at j ^ (co % 8)).
+template <typename T>
+__global__ void weight_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wsw, int G, int Cog,
+                                      int Cig, int T_) {
+  const int nkc = (Cig / BK) * T_;
+  const long long total = (long long)G * nkc * Cog * BK;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(e % BK);
+    long long r = e / BK;
+    const int co = (int)(r % Cog);
+    r /= Cog;
+    const int kc = (int)(r % nkc);
+    const int grp = (int)(r / nkc);
+    const int t = kc % T_, cc = kc / T_;
+    const int c = cc * BK + j;
+    const T v = w[((long long)(grp * Cog + co) * Cig + c) * T_ + t];
+    const long long blk = ((long long)grp * nkc + kc) * Cog * BK;
+    wsw[blk + (long long)co * BK + (((j >> 3) ^ (co & 7)) << 3) + (j & 7)] = v;
+  }
+}
+
+// Pipeline depth: as many stages (<= 4) as fit one CTA per SM (the kernel's
+// register use keeps it at one CTA per SM).
+int pick_stages(int Cog) {
+  const int stage = A_STAGE_BYTES + Cog * 128;
+  int s = (225 * 1024 - 2048) / stage;
+  return s > 4 ? 4 : s;
+}
+
+uint32_t tmem_cols_for(int n) {
+  uint32_t c = 32;
+  while ((int)c < n) c <<= 1;
+  return c;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- host side
+bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
+  if (d.dtype != DCN_BFLOAT16 && d.dtype != DCN_FLOAT16) return false;
+  if (g.Cig % BK != 0) return false;                 // K chunks of 64 channels inside one group
+  if (g.cpo % 8 != 0) return false;                  // 16-byte vectors inside one offset group
+  if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N tile: two epilogue halves of x16 loads
+  if (pick_stages(g.Cog) < 2) return false;
+  return true;
+}
+
+bool tc_backward_supported(const dcn_conv_desc&, const Geom&) { return false; }
+
+struct FwdWs {
+  size_t xh, wsw, total;
+};
+static FwdWs fwd_ws(const Geom& g, size_t es) {
+  FwdWs L;
+  L.xh = 0;
+  L.wsw = ws_align(es * (size_t)g.B * g.C * g.H * g.W);
+  L.total = L.wsw + ws_align(es * (size_t)g.Co * g.Cig * g.T);
+  return L;
+}
+
+size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g) {
+  return fwd_ws(g, 2).total;
+}
+size_t tc_backward_workspace(const dcn_conv_desc&, const Geom&) { return 0; }
+
+static int* status_ptr() {
+  static int* p = nullptr;
+  if (!p) {
+    void* q = nullptr;
+    if (cudaGetSymbolAddress(&q, sm100::g_dcn_status) == cudaSuccess) p = static_cast<int*>(q);
+  }
+  return p;
+}
+
+template <typename T>
+static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
+                                const T* bias, T* out, void* workspace, cudaStream_t st) {
+  const FwdWs L = fwd_ws(g, sizeof(T));
+  T* xh = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.xh);
+  T* wsw = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.wsw);
+  cudaError_t e;
+  {
+    KernelScope ks("nchw_to_nhwc", st);
+    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
+    nchw_to_nhwc_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  {
+    KernelScope ks("weight_swizzle", st);
+    const long long total = (long long)g.Co * g.Cig * g.T;
+    int blocks = (int)((total + 255) / 256);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    weight_swizzle_kernel<T><<<blocks, 256, 0, st>>>(w, wsw, g.G, g.Cog, g.Cig, g.T);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  FwdArgs a;
+  a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.bias = bias; a.out = out; a.wsw = wsw;
+  a.status = status_ptr();
+  if (!a.status) return cudaErrorSymbolNotFound;
+  a.g = g;
+  a.nkc = (g.Cig / BK) * g.T;
+  a.stages = pick_stages(g.Cog);
+  a.n_mma = (g.Cog + 255) / 256;
+  a.idesc = idesc_f16(BM, g.Cog / a.n_mma, std::is_same<T, __nv_bfloat16>::value);
+  a.tmem_cols = tmem_cols_for(g.Cog);
+  const FwdSmem SL = fwd_smem_layout(g.Cog, a.stages);
+  const int smem = (int)SL.total + 1024;
+  if ((e = cudaFuncSetAttribute(dcn_fwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem)) != cudaSuccess)
+    return e;
+  dim3 grid((unsigned)((g.P + BM - 1) / BM), (unsigned)g.G);
+  {
+    KernelScope ks("dcn_fwd_tc", st);
+    dcn_fwd_tc_kernel<T><<<grid, NTHREADS, smem, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
+                       const void* offset, const void* mask, const void* bias, void* output,
+                       void* workspace, cudaStream_t st) {
+  if (d.dtype == DCN_BFLOAT16)
+    return tc_forward_t<__nv_bfloat16>(g, (const __nv_bfloat16*)input, (const __nv_bfloat16*)weight,
+                                       (const __nv_bfloat16*)offset, (const __nv_bfloat16*)mask,
+                                       (const __nv_bfloat16*)bias, (__nv_bfloat16*)output, workspace, st);
+  return tc_forward_t<__half>(g, (const __half*)input, (const __half*)weight, (const __half*)offset,
+                              (const __half*)mask, (const __half*)bias, (__half*)output, workspace, st);
+}
+
 cudaError_t tc_backward(const dcn_conv_desc&, const Geom&, const void*, const void*, const void*,
                         const void*, const void*, void*, void*, void*, void*, void*, void*,
                         cudaStream_t) {
@@ -20,12 +488,12 @@ cudaError_t tc_backward(const dcn_conv_desc&, const Geom&, const void*, const vo
 }
 
 cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st) {
-  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_dcn_status, sizeof(int), 0,
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, sm100::g_dcn_status, sizeof(int), 0,
                                             cudaMemcpyDeviceToHost, st);
   if (e != cudaSuccess) return e;
   if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
   const int zero = 0;
-  return cudaMemcpyToSymbol(g_dcn_status, &zero, sizeof(int));
+  return cudaMemcpyToSymbol(sm100::g_dcn_status, &zero, sizeof(int));
 }
 
 }  // namespace dcn

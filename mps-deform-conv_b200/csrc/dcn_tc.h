@@ -6,9 +6,10 @@
 
 namespace dcn {
 
-// True when the tensor-core kernels handle this problem (fp16/bf16 and the
-// channel/size constraints listed in dcn_tc.cu).
-bool tc_supported(const dcn_conv_desc& d, const Geom& g);
+// True when the tensor-core kernels handle this problem's forward / backward
+// (fp16/bf16 and the channel constraints listed in dcn_tc.cu).
+bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g);
+bool tc_backward_supported(const dcn_conv_desc& d, const Geom& g);
 size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g);
 size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g);
 cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,

@@ -1,0 +1,98 @@
+"""Parity of the tensor-core (tcgen05) path: shapes whose channel counts the
+tcgen05 kernels take (per-group input channels a multiple of 64), fp16 and
+bf16, against the float64 oracle on the same rounded inputs.  Tolerance:
+normwise relative error <= 1e-2 (tests/_util.rel_err)."""
+import numpy as np
+import pytest
+import torch
+
+from _util import TOL, rel_err, to_np
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16}
+
+# (B, C, H, W, Co, groups, og, k, stride, pad, dil, mask, bias, offset_scale)
+SHAPES = {
+    "c64_og1": (2, 64, 12, 10, 64, 1, 1, 3, 1, 1, 1, True, True, 2.0),
+    "c64_og8_far": (2, 64, 9, 11, 64, 1, 8, 3, 1, 1, 1, True, False, 10.0),
+    "c128_g2_og4_dil2": (2, 128, 10, 10, 128, 2, 4, 3, 1, 2, 2, True, True, 3.0),
+    "c128_co256_s2": (1, 128, 14, 13, 256, 1, 1, 3, 2, 1, 1, True, False, 1.5),
+    "c64_co512_nomask": (1, 64, 8, 9, 512, 1, 1, 3, 1, 1, 1, False, True, 1.0),
+    "c192_co96_tail": (3, 192, 7, 9, 96, 1, 2, 3, 1, 1, 1, True, True, 2.0),
+}
+
+
+def _make(spec, dtype, dev, seed=0):
+    B, C, H, W, Co, G, og, k, s, p, d, use_mask, use_bias, osc = spec
+    g = torch.Generator().manual_seed(seed)
+    Ho = (H + 2 * p - (d * (k - 1) + 1)) // s + 1
+    Wo = (W + 2 * p - (d * (k - 1) + 1)) // s + 1
+    x = torch.randn(B, C, H, W, generator=g)
+    w = torch.randn(Co, C // G, k, k, generator=g) / np.sqrt(C // G * k * k)
+    off = torch.randn(B, 2 * og * k * k, Ho, Wo, generator=g) * osc
+    m = torch.sigmoid(torch.randn(B, og * k * k, Ho, Wo, generator=g)) if use_mask else None
+    b = torch.randn(Co, generator=g) * 0.1 if use_bias else None
+    go = torch.randn(B, Co, Ho, Wo, generator=g)
+    cv = lambda t: None if t is None else t.to(dev, dtype)
+    return dict(input=cv(x), weight=cv(w), offset=cv(off), mask=cv(m), bias=cv(b), grad_output=cv(go),
+                stride=(s, s), padding=(p, p), dilation=(d, d))
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_tc_forward_vs_oracle(name, dtype, cuda):
+    import mps_deform_conv as mdc
+    from mps_deform_conv import _abi
+    T = _make(SHAPES[name], DTYPES[dtype], cuda)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    lib = mdc._get_lib()
+    G = T["input"].shape[1] // T["weight"].shape[1]
+    og = T["offset"].shape[1] // 18
+    assert lib.uses_tensor_cores(T["input"], T["weight"], st[0], st[1], pd[0], pd[1], dl[0], dl[1],
+                                 G, og, T["mask"] is not None)
+    out = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    torch.cuda.synchronize()
+    lib.device_status()
+    ref = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    assert rel_err(to_np(out), ref) <= TOL[dtype]
+    # and through the public autograd API
+    out2 = mdc.deform_conv2d(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    assert rel_err(to_np(out2), ref) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_tc_backward_vs_oracle(name, dtype, cuda):
+    from mps_deform_conv import _abi
+    T = _make(SHAPES[name], DTYPES[dtype], cuda, seed=1)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    gi, goff, gw, gb, gm = _abi.call_backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                              st, pd, dl, T["mask"], with_bias=T["bias"] is not None)
+    torch.cuda.synchronize()
+    rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                                st, pd, dl, T["mask"], T["bias"] is not None)
+    tol = TOL[dtype]
+    assert rel_err(to_np(gi), rgi) <= tol
+    assert rel_err(to_np(goff), rgoff) <= tol
+    assert rel_err(to_np(gw), rgw) <= tol
+    if T["bias"] is not None:
+        assert rel_err(to_np(gb), rgb) <= tol
+    if T["mask"] is not None:
+        assert rel_err(to_np(gm), rgm) <= tol
+
+
+def test_tc_forward_deterministic_and_batch_consistent(cuda):
+    """Forward has no atomics: repeated runs are bitwise equal, and a batch
+    slice gives the same rows as the full batch."""
+    from mps_deform_conv import _abi
+    T = _make(SHAPES["c128_g2_og4_dil2"], torch.bfloat16, cuda, seed=3)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    a = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    b = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    c = _abi.call_forward(T["input"][1:].contiguous(), T["offset"][1:].contiguous(), T["weight"],
+                          T["bias"], st, pd, dl, T["mask"][1:].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(a[1:], c)
