@@ -23,12 +23,12 @@
 // the device status word and unwinds.
 #include <type_traits>
 
-#include "dcn_sm100.cuh"
-#include "dcn_tc.h"
+#include "dcn_tc_common.cuh"
 
 namespace dcn {
 
 using namespace sm100;
+using namespace tcc;
 
 namespace sm100 {
 // Device status word: set by a kernel whose bounded wait expired.
@@ -37,38 +37,14 @@ __device__ int g_dcn_status = 0;
 
 namespace {
 
-constexpr int BM = 128;           // pixels per tile (MMA M)
-constexpr int BK = 64;            // channels per K chunk (one 128-byte row)
 constexpr int NPROD_WARPS = 8;
 constexpr int NPROD = NPROD_WARPS * 32;
 constexpr int MMA_WARP = 8;
 constexpr int LOAD_WARP = 9;
 constexpr int NTHREADS = 320;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 
 // status codes recorded on a wait that expired
 constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16;
-
-template <typename T> struct Vec;
-template <> struct Vec<__nv_bfloat16> {
-  static __device__ __forceinline__ float2 unpack(uint32_t w) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-  }
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-};
-template <> struct Vec<__half> {
-  static __device__ __forceinline__ float2 unpack(uint32_t w) {
-    __half2 h = *reinterpret_cast<__half2*>(&w);
-    return __half22float2(h);
-  }
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-};
 
 struct FwdSmem {  // offsets within the 1024-aligned dynamic shared memory
   uint32_t a, b, bar, total;
@@ -103,72 +79,6 @@ struct FwdArgs {
   uint32_t idesc;     // instruction descriptor for N = Cog / n_mma
   uint32_t tmem_cols;
 };
-
-// ---------------------------------------------------------------- producer
-// Gathers one K chunk (tap t, 64 channels starting at c_abs0) of pixel row r
-// for this thread's 4 channel vectors [v0, v0+4) into the swizzled A row.
-template <typename T>
-__device__ __forceinline__ void gather_row(const FwdArgs& a, const T* __restrict__ xh,
-                                           const T* __restrict__ off, const T* __restrict__ msk,
-                                           uint8_t* arow, int r, int v0, bool valid, int b, int p,
-                                           int t, int c_abs0) {
-  const Geom& g = a.g;
-  uint4 vals[4][4];
-  float wts[4][4];
-  int cur_o = -1;
-  float w4[4] = {0.f, 0.f, 0.f, 0.f};
-  long long base4[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    const int c_abs = c_abs0 + (v0 + v) * 8;
-    if (valid) {
-      const int o = c_abs / g.cpo;
-      if (o != cur_o) {
-        cur_o = o;
-        float y, x, m;
-        sample_point(g, off, msk, b, o, t, p, &y, &x, &m);
-        const Corners cs = corners_of(y, x, g.H, g.W);
-        const long long img = (long long)b * g.H * g.W;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          w4[k] = cs.w[k] * m;
-          base4[k] = (img + cs.idx[k]) * g.C;
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        wts[v][k] = w4[k];
-        vals[v][k] = (w4[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(xh + base4[k] + c_abs))
-                                    : make_uint4(0, 0, 0, 0);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        wts[v][k] = 0.f;
-        vals[v][k] = make_uint4(0, 0, 0, 0);
-      }
-    }
-  }
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&vals[v][0]);
-    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&vals[v][1]);
-    const uint32_t* q2 = reinterpret_cast<const uint32_t*>(&vals[v][2]);
-    const uint32_t* q3 = reinterpret_cast<const uint32_t*>(&vals[v][3]);
-    uint32_t o4[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f0 = Vec<T>::unpack(q0[e]), f1 = Vec<T>::unpack(q1[e]);
-      const float2 f2 = Vec<T>::unpack(q2[e]), f3 = Vec<T>::unpack(q3[e]);
-      const float lo = wts[v][0] * f0.x + wts[v][1] * f1.x + wts[v][2] * f2.x + wts[v][3] * f3.x;
-      const float hi = wts[v][0] * f0.y + wts[v][1] * f1.y + wts[v][2] * f2.y + wts[v][3] * f3.y;
-      o4[e] = Vec<T>::pack(lo, hi);
-    }
-    const int chunk = v0 + v;
-    uint4* dst = reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4));
-    *dst = make_uint4(o4[0], o4[1], o4[2], o4[3]);
-  }
-}
 
 template <typename T>
 __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a) {
@@ -229,7 +139,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
       ok = mbar_wait(empty(s), parity, abort_flag, a.status, ST_PROD);
       if (!ok) break;
       const int t = i % g.T, cc = i / g.T;
-      gather_row<T>(a, xh, off, msk, smem + L.a + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
+      gather_row<T>(g, xh, off, msk, smem + L.a + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
                     t, grp * g.Cig + cc * BK);
       fence_async_shared();
       mbar_arrive(a_full(s));
@@ -398,8 +308,6 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   return true;
 }
 
-bool tc_backward_supported(const dcn_conv_desc&, const Geom&) { return false; }
-
 struct FwdWs {
   size_t xh, wsw, total;
 };
@@ -414,15 +322,39 @@ static FwdWs fwd_ws(const Geom& g, size_t es) {
 size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g) {
   return fwd_ws(g, 2).total;
 }
-size_t tc_backward_workspace(const dcn_conv_desc&, const Geom&) { return 0; }
 
-static int* status_ptr() {
-  static int* p = nullptr;
+int* tc_status_ptr() {
+  static int* p = nullptr;  // one device address per process (first device that asks)
   if (!p) {
     void* q = nullptr;
     if (cudaGetSymbolAddress(&q, sm100::g_dcn_status) == cudaSuccess) p = static_cast<int*>(q);
   }
   return p;
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
+                  uint32_t box_rows, uint32_t box_cols) {
+  typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                               CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                               CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    encode = reinterpret_cast<EncodeFn>(fn);
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <typename T>
@@ -449,7 +381,7 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
 
   FwdArgs a;
   a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.bias = bias; a.out = out; a.wsw = wsw;
-  a.status = status_ptr();
+  a.status = tc_status_ptr();
   if (!a.status) return cudaErrorSymbolNotFound;
   a.g = g;
   a.nkc = (g.Cig / BK) * g.T;
@@ -481,11 +413,6 @@ cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input,
                               (const __half*)mask, (const __half*)bias, (__half*)output, workspace, st);
 }
 
-cudaError_t tc_backward(const dcn_conv_desc&, const Geom&, const void*, const void*, const void*,
-                        const void*, const void*, void*, void*, void*, void*, void*, void*,
-                        cudaStream_t) {
-  return cudaErrorNotSupported;
-}
 
 cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st) {
   cudaError_t e = cudaMemcpyFromSymbolAsync(out, sm100::g_dcn_status, sizeof(int), 0,

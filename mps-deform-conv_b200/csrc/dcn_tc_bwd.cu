@@ -1,0 +1,733 @@
+// dcn_tc_bwd.cu -- tensor-core (tcgen05 / TMEM) backward for sm_100a.
+//
+// The reference's backward (mps_deform_conv/__init__.py:245-322) recomputes the
+// column buffer, runs two torch.mm GEMMs and two scatter/reduce kernels
+// (deform_conv2d_mps.mm:344-519).  Here:
+//
+//   prep        grad_output NCHW -> pixel-major gOt[P][Co] (+ grad_bias sums),
+//               input -> channels-last, weight -> W^T tiles for dgrad.
+//   dgrad       (dcn_dgrad_tc_kernel) per 128-pixel tile: gcol = gOt . W^T on
+//               tcgen05 into TMEM, one 64-channel K chunk (tap, channels) at a
+//               time; the epilogue reads each gcol tile from TMEM and, without
+//               writing it anywhere, (a) gathers the 4 bilinear corners of the
+//               input to reduce the offset and mask gradients over channels
+//               (col2im_coord, mm:423-519) and (b) scatters mask * weight *
+//               gcol into an fp32 channels-last grad_input with vector
+//               red.global.add.v4.f32 (col2im, mm:344-417).
+//   wgrad       (dcn_wgrad_tc_kernel) gW[co][k] = sum_p gOt[p][co] col[p][k]:
+//               the forward's gather producer rebuilds col tiles in shared
+//               memory as the MN-major B operand, gOt tiles arrive by TMA as
+//               the MN-major A operand; each CTA owns a few K chunks and a
+//               range of pixel tiles, accumulates in TMEM and adds its partial
+//               gW into an fp32 buffer.
+//   finalize    fp32 accumulators -> caller dtype / NCHW.
+#include "dcn_tc_common.cuh"
+
+namespace dcn {
+
+using namespace sm100;
+using namespace tcc;
+
+namespace {
+
+constexpr int ST_W_PROD = 21, ST_W_MMA = 22, ST_W_LOAD = 23, ST_W_EPI = 24, ST_W_DRAIN = 25;
+constexpr int ST_D_MMA = 31, ST_D_LOAD = 32, ST_D_EPI = 33, ST_D_DRAIN = 34;
+
+// ================================================================ wgrad
+constexpr int W_NPROD_WARPS = 8;
+constexpr int W_NPROD = W_NPROD_WARPS * 32;
+constexpr int W_MMA_WARP = 8;
+constexpr int W_NTHREADS = 320;
+
+struct WgradArgs {
+  const void* xh;
+  const void* off;
+  const void* msk;
+  float* gw32;     // [Co][Cig][T] fp32, zeroed
+  int* status;
+  Geom g;
+  int nkc;         // K chunks per group, kc = cc*T + t
+  int nkg;         // K chunks per CTA
+  int mh;          // M halves of 128 output channels
+  int ncb;         // 64-channel blocks of grad_output loaded per tile
+  int tiles_per_cta;
+  int n_tiles;
+  int a_stages, b_stages;
+  uint32_t idesc;
+  uint32_t tmem_cols;
+};
+
+struct WgradSmem {
+  uint32_t a, a_stage, b, bar, total;
+};
+__host__ __device__ inline WgradSmem wgrad_smem(int mh, int a_stages, int b_stages) {
+  WgradSmem L;
+  L.a = 0;
+  L.a_stage = (uint32_t)(2 * mh) * A_STAGE_BYTES;
+  L.b = L.a + a_stages * L.a_stage;
+  L.bar = L.b + b_stages * A_STAGE_BYTES;
+  L.total = L.bar + (2 * a_stages + 2 * b_stages + 2) * 8 + 16;
+  return L;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(W_NTHREADS, 1)
+dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Geom& g = a.g;
+  const int AS = a.a_stages, BS = a.b_stages;
+  const WgradSmem L = wgrad_smem(a.mh, AS, BS);
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + L.bar;
+  auto a_full = [&](int s) { return bar0 + 8u * s; };
+  auto a_empty = [&](int s) { return bar0 + 8u * (AS + s); };
+  auto b_full = [&](int s) { return bar0 + 8u * (2 * AS + s); };
+  auto b_empty = [&](int s) { return bar0 + 8u * (2 * AS + BS + s); };
+  const uint32_t d_full = bar0 + 8u * (2 * AS + 2 * BS);
+  const uint32_t drain = d_full + 8u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (2 * AS + 2 * BS + 2) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = blockIdx.y;
+  const int k0 = blockIdx.x * a.nkg;
+  const int nk = min(a.nkg, a.nkc - k0);
+  const int t0 = blockIdx.z * a.tiles_per_cta;
+  const int nt = max(0, min(a.tiles_per_cta, a.n_tiles - t0));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AS; ++s) { mbar_init(a_full(s), 1); mbar_init(a_empty(s), 1); }
+    for (int s = 0; s < BS; ++s) { mbar_init(b_full(s), W_NPROD); mbar_init(b_empty(s), 1); }
+    mbar_init(d_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == W_MMA_WARP) {
+    tmem_alloc(smem_addr(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const T* xh = static_cast<const T*>(a.xh);
+  const T* off = static_cast<const T*>(a.off);
+  const T* msk = static_cast<const T*>(a.msk);
+
+  if (warp < W_NPROD_WARPS) {
+    // -------------------------------------------- col-tile producers
+    const int r = threadIdx.x & (BM - 1);
+    const int v0 = (threadIdx.x >> 7) * 4;
+    bool ok = true;
+    for (int li = 0; li < nt && ok; ++li) {
+      const long long pix = (long long)(t0 + li) * BM + r;
+      const bool valid = pix < g.P;
+      const int b = valid ? (int)(pix / g.HWo) : 0;
+      const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
+      for (int kcl = 0; kcl < nk && ok; ++kcl) {
+        const int j = li * nk + kcl;
+        const int s = j % BS;
+        ok = mbar_wait(b_empty(s), ((j / BS) & 1) ^ 1, abort_flag, a.status, ST_W_PROD);
+        if (!ok) break;
+        const int kc = k0 + kcl;
+        const int t = kc % g.T, cc = kc / g.T;
+        gather_row<T>(g, xh, off, msk, smem + L.b + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
+                      t, grp * g.Cig + cc * BK);
+        fence_async_shared();
+        mbar_arrive(b_full(s));
+      }
+    }
+    // -------------------------------------------- epilogue: TMEM -> fp32 atomics
+    const bool ready = nt > 0 && ok && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
+    if (__all_sync(0xffffffffu, ready)) {
+      tc_fence_after();
+      const int q = warp & 3, half = warp >> 2;
+      for (int blk = half; blk < a.mh * nk; blk += 2) {
+        const int h = blk / nk, kcl = blk % nk;
+        const int co = h * BM + q * 32 + lane;
+        const int kc = k0 + kcl;
+        const int t = kc % g.T, cc = kc / g.T;
+        const uint32_t col = (uint32_t)((h * a.nkg + kcl) * 64);
+#pragma unroll 1
+        for (int c16 = 0; c16 < 4; ++c16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + col + c16 * 16, v);
+          tmem_ld_wait();
+          if (co < g.Cog) {
+            float* dst = a.gw32 + ((long long)(grp * g.Cog + co) * g.Cig + cc * BK + c16 * 16) * g.T + t;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) atomicAdd(dst + (long long)jj * g.T, __uint_as_float(v[jj]));
+          }
+        }
+      }
+    }
+  } else if (warp == W_MMA_WARP) {
+    // -------------------------------------------- MMA issuer
+    if (lane == 0 && nt > 0) {
+      bool ok = true;
+      int committed = 0;
+      for (int li = 0; li < nt && ok; ++li) {
+        const int as = li % AS;
+        ok = mbar_wait(a_full(as), (li / AS) & 1, abort_flag, a.status, ST_W_MMA);
+        if (!ok) break;
+        const uint32_t abase = sbase + L.a + as * L.a_stage;
+        for (int kcl = 0; kcl < nk && ok; ++kcl) {
+          const int j = li * nk + kcl;
+          const int s = j % BS;
+          ok = mbar_wait(b_full(s), (j / BS) & 1, abort_flag, a.status, ST_W_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t bbase = sbase + L.b + s * A_STAGE_BYTES;
+          for (int h = 0; h < a.mh; ++h) {
+            const uint32_t dcol = (uint32_t)((h * a.nkg + kcl) * 64);
+#pragma unroll
+            for (int kk = 0; kk < BM / 16; ++kk) {
+              const uint64_t ad = desc_mnmajor_sw128(abase + h * 2 * A_STAGE_BYTES + kk * 2048, A_STAGE_BYTES);
+              const uint64_t bd = desc_mnmajor_sw128(bbase + kk * 2048, A_STAGE_BYTES);
+              mma_f16(tmem + dcol, ad, bd, a.idesc, (li > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(b_empty(s));
+          ++committed;
+        }
+        if (ok) mma_commit(a_empty(as));
+      }
+      if (ok) {
+        mma_commit(d_full);
+      } else if (committed > 0) {
+        mma_commit(drain);
+        mbar_wait(drain, 0, abort_flag, a.status, ST_W_DRAIN);
+      }
+    }
+  } else {
+    // -------------------------------------------- grad_output tiles by TMA
+    if (lane == 0 && nt > 0) {
+      int issued = 0;
+      const uint32_t bytes = (uint32_t)a.ncb * A_STAGE_BYTES;
+      for (int li = 0; li < nt; ++li) {
+        const int s = li % AS;
+        if (!mbar_wait(a_empty(s), ((li / AS) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD)) break;
+        mbar_arrive_expect_tx(a_full(s), bytes);
+        const uint32_t dst = sbase + L.a + s * L.a_stage;
+        for (int cb = 0; cb < a.ncb; ++cb)
+          tma_load_2d(dst + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, (t0 + li) * BM, a_full(s));
+        ++issued;
+      }
+      for (int li = (issued > AS ? issued - AS : 0); li < issued; ++li)
+        mbar_wait(a_full(li % AS), (li / AS) & 1, abort_flag, a.status, ST_W_LOAD);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == W_MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+// ================================================================ dgrad
+constexpr int D_EPI_WARPS = 16;      // 4 groups of 4 warps, one group per TMEM buffer
+constexpr int D_MMA_WARP = 16;
+constexpr int D_LOAD_WARP = 17;
+constexpr int D_NTHREADS = 576;
+constexpr int D_NBUF = 4;            // TMEM gcol buffers of 64 columns
+
+struct DgradArgs {
+  const void* xh;
+  const void* off;
+  const void* msk;
+  const void* wdt;   // W^T tiles [G][NKC][KB][64 ch][64 co], 128-byte swizzled rows
+  float* gi32;       // channels-last [B][H][W][C], zeroed
+  float* goff32;     // [B][OG*2T][HWo], zeroed
+  float* gmsk32;     // [B][OG*T][HWo], zeroed (null without mask)
+  int* status;
+  Geom g;
+  int nkc;           // K chunks per group, kc = cc*T + t
+  int kb;            // 64-channel blocks of the reduction over output channels
+  int b_stages;
+  uint32_t idesc;
+};
+
+// Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
+// streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each.
+struct DgradSmem {
+  uint32_t a, b, b_stage, bar, total;
+};
+__host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages) {
+  DgradSmem L;
+  L.a = 0;
+  L.b = (uint32_t)kb * A_STAGE_BYTES;
+  L.b_stage = 8192u;
+  L.bar = L.b + b_stages * L.b_stage;
+  L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
+  return L;
+}
+
+__device__ __forceinline__ void red_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(D_NTHREADS, 1)
+dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Geom& g = a.g;
+  const int S = a.b_stages;
+  const DgradSmem L = dgrad_smem(a.kb, S);
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + L.bar;
+  const uint32_t a_full = bar0;
+  auto b_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto b_empty = [&](int s) { return bar0 + 8u * (1 + S + s); };
+  auto d_full = [&](int e) { return bar0 + 8u * (1 + 2 * S + e); };
+  auto d_empty = [&](int e) { return bar0 + 8u * (1 + 2 * S + D_NBUF + e); };
+  const uint32_t drain = bar0 + 8u * (1 + 2 * S + 2 * D_NBUF);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (1 + 2 * S + 2 * D_NBUF + 1) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, grp = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int s = 0; s < S; ++s) { mbar_init(b_full(s), 1); mbar_init(b_empty(s), 1); }
+    for (int e = 0; e < D_NBUF; ++e) { mbar_init(d_full(e), 1); mbar_init(d_empty(e), 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == D_MMA_WARP) {
+    tmem_alloc(smem_addr(tmem_slot), 64 * D_NBUF);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < D_EPI_WARPS) {
+    // -------------------------------------------- epilogue: col2im + col2im_coord
+    const T* xh = static_cast<const T*>(a.xh);
+    const T* off = static_cast<const T*>(a.off);
+    const T* msk = static_cast<const T*>(a.msk);
+    const int e = warp >> 2, q = warp & 3;
+    const int r = q * 32 + lane;
+    const long long pix = (long long)tile * BM + r;
+    const bool valid = pix < g.P;
+    const int b = valid ? (int)(pix / g.HWo) : 0;
+    const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
+    const long long img = (long long)b * g.H * g.W;
+    bool ok = true;
+    for (int i = e; i < a.nkc; i += D_NBUF) {
+      const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
+      ok = __all_sync(0xffffffffu, ready);
+      if (!ok) break;
+      tc_fence_after();
+      const int t = i % g.T, cc = i / g.T;
+      const int cbase = grp * g.Cig + cc * BK;
+      int cur_o = -1;
+      float m = 0.f, fy = 0.f, fx = 0.f;
+      float wb[4] = {0.f, 0.f, 0.f, 0.f};    // bilinear weights (0 outside / invalid)
+      bool cv[4] = {false, false, false, false};  // corner in bounds (coordinate derivative)
+      long long cbase4[4] = {0, 0, 0, 0};
+      float gy = 0.f, gx = 0.f, gm = 0.f;
+      auto flush = [&](int o) {
+        if (o < 0 || !valid) return;
+        const long long ob = ((long long)(b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + p;
+        atomicAdd(a.goff32 + ob, m * gy);
+        atomicAdd(a.goff32 + ob + g.HWo, m * gx);
+        if (g.use_mask) atomicAdd(a.gmsk32 + ((long long)(b * g.OG + o) * g.T + t) * g.HWo + p, gm);
+        gy = gx = gm = 0.f;
+      };
+#pragma unroll 1
+      for (int sub = 0; sub < 4; ++sub) {
+        uint32_t acc[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64 + sub * 16), acc);
+        tmem_ld_wait();
+        if (!valid) continue;
+#pragma unroll
+        for (int v2 = 0; v2 < 2; ++v2) {
+          const int c_abs = cbase + sub * 16 + v2 * 8;
+          const int o = c_abs / g.cpo;
+          if (o != cur_o) {
+            flush(cur_o);
+            cur_o = o;
+            float y, x;
+            sample_point(g, off, msk, b, o, t, p, &y, &x, &m);
+            const Corners cs = corners_of(y, x, g.H, g.W);
+            const CoordCorners cc4 = coord_corners_of(y, x, g.H, g.W);
+            fy = cc4.fy;
+            fx = cc4.fx;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              wb[k] = cs.w[k];
+              cv[k] = cc4.v[k];
+              cbase4[k] = (img + cc4.idx[k]) * g.C;
+            }
+          }
+          uint4 xv[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            xv[k] = cv[k] ? __ldg(reinterpret_cast<const uint4*>(xh + cbase4[k] + c_abs)) : make_uint4(0, 0, 0, 0);
+          float gv[8];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) gv[jj] = __uint_as_float(acc[v2 * 8 + jj]);
+#pragma unroll
+          for (int w2 = 0; w2 < 4; ++w2) {
+            const float2 f0 = Vec<T>::unpack((&xv[0].x)[w2]);
+            const float2 f1 = Vec<T>::unpack((&xv[1].x)[w2]);
+            const float2 f2 = Vec<T>::unpack((&xv[2].x)[w2]);
+            const float2 f3 = Vec<T>::unpack((&xv[3].x)[w2]);
+            const float ga = gv[2 * w2], gb = gv[2 * w2 + 1];
+            gm += ga * (wb[0] * f0.x + wb[1] * f1.x + wb[2] * f2.x + wb[3] * f3.x);
+            gm += gb * (wb[0] * f0.y + wb[1] * f1.y + wb[2] * f2.y + wb[3] * f3.y);
+            gy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
+            gy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
+            gx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
+            gx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float wk = wb[k] * m;
+            if (wk != 0.f) {
+              float* dst = a.gi32 + cbase4[k] + c_abs;
+              red_v4(dst, wk * gv[0], wk * gv[1], wk * gv[2], wk * gv[3]);
+              red_v4(dst + 4, wk * gv[4], wk * gv[5], wk * gv[6], wk * gv[7]);
+            }
+          }
+        }
+      }
+      flush(cur_o);
+      tc_fence_before();
+      mbar_arrive(d_empty(e));
+    }
+  } else if (warp == D_MMA_WARP) {
+    // -------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(a_full, 0, abort_flag, a.status, ST_D_MMA);
+      int committed = 0;
+      for (int i = 0; i < a.nkc && ok; ++i) {
+        const int e = i % D_NBUF;
+        ok = mbar_wait(d_empty(e), ((i / D_NBUF) & 1) ^ 1, abort_flag, a.status, ST_D_MMA);
+        for (int kb = 0; kb < a.kb && ok; ++kb) {
+          const int j = i * a.kb + kb, s = j % S;
+          ok = mbar_wait(b_full(s), (j / S) & 1, abort_flag, a.status, ST_D_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t bbase = sbase + L.b + s * L.b_stage;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const uint64_t ad = desc_kmajor_sw128(sbase + L.a + kb * A_STAGE_BYTES + k4 * 32);
+            const uint64_t bd = desc_kmajor_sw128(bbase + k4 * 32);
+            mma_f16(tmem + (uint32_t)(e * 64), ad, bd, a.idesc, (kb > 0 || k4 > 0) ? 1u : 0u);
+          }
+          mma_commit(b_empty(s));
+          ++committed;
+        }
+        if (ok) mma_commit(d_full(e));
+      }
+      if (!ok && committed > 0) {
+        mma_commit(drain);
+        mbar_wait(drain, 0, abort_flag, a.status, ST_D_DRAIN);
+      }
+    }
+  } else {
+    // -------------------------------------------- loader: gOt tile (TMA) + W^T tiles (bulk)
+    if (lane == 0) {
+      mbar_arrive_expect_tx(a_full, (uint32_t)a.kb * A_STAGE_BYTES);
+      for (int cb = 0; cb < a.kb; ++cb)
+        tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, tile * BM, a_full);
+      // K blocks of W^T in order (kc, kb): block j = kc*KB + kb
+      const uint8_t* wbase = static_cast<const uint8_t*>(a.wdt) + (size_t)grp * a.nkc * a.kb * L.b_stage;
+      int issued = 0;
+      for (int j = 0; j < a.nkc * a.kb; ++j) {
+        const int s = j % S;
+        if (!mbar_wait(b_empty(s), ((j / S) & 1) ^ 1, abort_flag, a.status, ST_D_LOAD)) break;
+        mbar_arrive_expect_tx(b_full(s), L.b_stage);
+        bulk_g2s(sbase + L.b + s * L.b_stage, wbase + (size_t)j * L.b_stage, L.b_stage, b_full(s));
+        ++issued;
+      }
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+        mbar_wait(b_full(i % S), (i / S) & 1, abort_flag, a.status, ST_D_LOAD);
+      mbar_wait(a_full, 0, abort_flag, a.status, ST_D_LOAD);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == D_MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64 * D_NBUF);
+  }
+}
+
+// ================================================================ prep / finalize
+// grad_output NCHW [B][Co][HWo] -> gOt [B*HWo][Co]; gb32[co] += tile sums.
+template <typename T>
+__global__ void go_transpose_bias_kernel(const T* __restrict__ go, T* __restrict__ got,
+                                         float* __restrict__ gb32, int Co, int HW) {
+  __shared__ float tile[64][65];
+  const int b = blockIdx.z, c0 = blockIdx.y * 64, hw0 = blockIdx.x * 64;
+  const T* src = go + (long long)b * Co * HW;
+  T* dst = got + (long long)b * HW * Co;
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int cc = e / 64, hh = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    tile[cc][hh] = (c < Co && hw < HW) ? to_f(src[(long long)c * HW + hw]) : 0.f;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int hh = e / 64, cc = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < Co && hw < HW) dst[(long long)hw * Co + c] = from_f<T>(tile[cc][hh]);
+  }
+  if (gb32 && threadIdx.x < 64 && c0 + threadIdx.x < Co) {
+    float s = 0.f;
+    for (int hh = 0; hh < 64; ++hh) s += tile[threadIdx.x][hh];
+    atomicAdd(gb32 + c0 + threadIdx.x, s);
+  }
+}
+
+// weight [Co][Cig][T] -> W^T tiles [G][NKC][KB][64 ch][64 co]: row = channel j
+// of K chunk kc = (cc, t), 64 output channels per 128-byte row, chunk
+// ((co % 64) / 8) of row j stored at position ^ (j % 8); co >= Cog are zero.
+template <typename T>
+__global__ void weight_t_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wdt, int G, int Cog,
+                                        int Cig, int T_, int KB) {
+  const int nkc = (Cig / BK) * T_;
+  const long long total = (long long)G * nkc * KB * 64 * 64;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int col = (int)(e % 64);          // output channel within block (logical)
+    long long r = e / 64;
+    const int j = (int)(r % 64);            // channel within K chunk
+    r /= 64;
+    const int kb = (int)(r % KB);
+    r /= KB;
+    const int kc = (int)(r % nkc);
+    const int grp = (int)(r / nkc);
+    const int co = kb * 64 + col;
+    const int t = kc % T_, cc = kc / T_;
+    const int c = cc * BK + j;
+    const T v = co < Cog ? w[((long long)(grp * Cog + co) * Cig + c) * T_ + t] : from_f<T>(0.f);
+    const long long blk = (((long long)grp * nkc + kc) * KB + kb) * 4096;
+    wdt[blk + j * 64 + (((col >> 3) ^ (j & 7)) << 3) + (col & 7)] = v;
+  }
+}
+
+// channels-last fp32 [B][HW][C] -> NCHW T [B][C][HW].
+template <typename T>
+__global__ void nhwc_f32_to_nchw_kernel(const float* __restrict__ src, T* __restrict__ dst, int C, int HW) {
+  __shared__ float tile[64][65];
+  const int b = blockIdx.z, c0 = blockIdx.y * 64, hw0 = blockIdx.x * 64;
+  const float* s = src + (long long)b * HW * C;
+  T* d = dst + (long long)b * C * HW;
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int hh = e / 64, cc = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) tile[cc][hh] = s[(long long)hw * C + c];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int cc = e / 64, hh = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) d[(long long)c * HW + hw] = from_f<T>(tile[cc][hh]);
+  }
+}
+
+template <typename T>
+__global__ void nchw_to_nhwc_bwd_kernel(const T* __restrict__ x, T* __restrict__ xh, int C, int HW) {
+  __shared__ T tile[64][65];
+  const int b = blockIdx.z, c0 = blockIdx.y * 64, hw0 = blockIdx.x * 64;
+  const T* src = x + (long long)b * C * HW;
+  T* dst = xh + (long long)b * C * HW;
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int cc = e / 64, hh = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) tile[cc][hh] = src[(long long)c * HW + hw];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int hh = e / 64, cc = e % 64;
+    const int c = c0 + cc, hw = hw0 + hh;
+    if (c < C && hw < HW) dst[(long long)hw * C + c] = tile[cc][hh];
+  }
+}
+
+// ================================================================ host
+struct BwdWs {
+  size_t xh, got, wdt, acc, gi32, goff32, gmsk32, gw32, gb32, acc_bytes, total;
+};
+BwdWs bwd_ws(const Geom& g, size_t es) {
+  BwdWs L;
+  const int KB = (g.Cog + 63) / 64;
+  const int nkc = (g.Cig / BK) * g.T;
+  size_t o = 0;
+  L.xh = o;   o += ws_align(es * (size_t)g.B * g.H * g.W * g.C);
+  L.got = o;  o += ws_align(es * (size_t)g.P * g.Co);
+  L.wdt = o;  o += ws_align(es * (size_t)g.G * nkc * KB * 4096);
+  L.acc = o;  // fp32 accumulators, contiguous so one memset clears them
+  L.gi32 = o;   o += ws_align(4 * (size_t)g.B * g.H * g.W * g.C);
+  L.goff32 = o; o += ws_align(4 * (size_t)g.B * g.OG * 2 * g.T * g.HWo);
+  L.gmsk32 = o; o += ws_align(4 * (size_t)g.B * g.OG * g.T * g.HWo);
+  L.gw32 = o;   o += ws_align(4 * (size_t)g.Co * g.Cig * g.T);
+  L.gb32 = o;   o += ws_align(4 * (size_t)g.Co);
+  L.acc_bytes = o - L.acc;
+  L.total = o;
+  return L;
+}
+
+uint32_t pow2_cols(int n) {
+  uint32_t c = 32;
+  while ((int)c < n) c <<= 1;
+  return c;
+}
+
+static int grid_cap(long long n) {
+  long long b = (n + 255) / 256;
+  return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
+}
+
+template <typename T>
+cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, const T* off, const T* msk,
+                          T* gin, T* gw, T* goff, T* gmsk, T* gb, void* workspace, cudaStream_t st) {
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const BwdWs L = bwd_ws(g, sizeof(T));
+  char* ws = static_cast<char*>(workspace);
+  T* xh = reinterpret_cast<T*>(ws + L.xh);
+  T* got = reinterpret_cast<T*>(ws + L.got);
+  T* wdt = reinterpret_cast<T*>(ws + L.wdt);
+  float* gi32 = reinterpret_cast<float*>(ws + L.gi32);
+  float* goff32 = reinterpret_cast<float*>(ws + L.goff32);
+  float* gmsk32 = reinterpret_cast<float*>(ws + L.gmsk32);
+  float* gw32 = reinterpret_cast<float*>(ws + L.gw32);
+  float* gb32 = reinterpret_cast<float*>(ws + L.gb32);
+  int* status = tc_status_ptr();
+  if (!status) return cudaErrorSymbolNotFound;
+  const bool need_d = gin || goff || gmsk;
+  const int KB = (g.Cog + 63) / 64;
+  const int nkc = (g.Cig / BK) * g.T;
+  const int n_tiles = (int)((g.P + BM - 1) / BM);
+  cudaError_t e;
+
+  if ((e = cudaMemsetAsync(ws + L.acc, 0, L.acc_bytes, st)) != cudaSuccess) return e;
+  {
+    KernelScope ks("go_transpose_bias", st);
+    dim3 grid((g.HWo + 63) / 64, (g.Co + 63) / 64, g.B);
+    go_transpose_bias_kernel<T><<<grid, 256, 0, st>>>(go, got, gb ? gb32 : nullptr, g.Co, g.HWo);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  {
+    KernelScope ks("nchw_to_nhwc", st);
+    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
+    nchw_to_nhwc_bwd_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  CUtensorMap tmap;
+  if (!make_tmap_2d(&tmap, got, bf16, (uint64_t)g.P, (uint64_t)g.Co, BM, 64)) return cudaErrorInvalidValue;
+
+  if (need_d) {
+    {
+      KernelScope ks("weight_t_swizzle", st);
+      weight_t_swizzle_kernel<T><<<grid_cap((long long)g.G * nkc * KB * 4096), 256, 0, st>>>(
+          w, wdt, g.G, g.Cog, g.Cig, g.T, KB);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    DgradArgs a;
+    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.wdt = wdt;
+    a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
+    a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
+    a.b_stages = 8;
+    while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) --a.b_stages;
+    if (dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
+    a.idesc = idesc_f16(BM, 64, bf16);
+    const int smem = (int)dgrad_smem(KB, a.b_stages).total + 1024;
+    if ((e = cudaFuncSetAttribute(dcn_dgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      return e;
+    KernelScope ks("dcn_dgrad_tc", st);
+    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G), D_NTHREADS, smem, st>>>(a, tmap);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (gw) {
+    WgradArgs a;
+    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.gw32 = gw32;
+    a.status = status; a.g = g; a.nkc = nkc;
+    a.mh = (g.Cog + BM - 1) / BM;
+    const int nkg_max = 8 / a.mh;  // TMEM: mh * nkg * 64 columns <= 512
+    const int ngroups = (nkc + nkg_max - 1) / nkg_max;
+    a.nkg = (nkc + ngroups - 1) / ngroups;
+    a.ncb = (g.Cog + 63) / 64;
+    const int kgroups = (nkc + a.nkg - 1) / a.nkg;
+    const int base = kgroups * g.G;
+    int splits = (2 * 148 + base - 1) / base;
+    if (splits > n_tiles) splits = n_tiles;
+    if (splits < 1) splits = 1;
+    a.tiles_per_cta = (n_tiles + splits - 1) / splits;
+    splits = (n_tiles + a.tiles_per_cta - 1) / a.tiles_per_cta;
+    a.n_tiles = n_tiles;
+    a.b_stages = 4;
+    a.a_stages = 2;
+    while (wgrad_smem(a.mh, a.a_stages, a.b_stages).total + 1024 > 225 * 1024) {
+      if (a.b_stages > 2) --a.b_stages;
+      else if (a.a_stages > 1) --a.a_stages;
+      else return cudaErrorInvalidConfiguration;
+    }
+    a.idesc = idesc_f16_major(BM, 64, bf16, true, true);
+    a.tmem_cols = pow2_cols(a.mh * a.nkg * 64);
+    const int smem = (int)wgrad_smem(a.mh, a.a_stages, a.b_stages).total + 1024;
+    if ((e = cudaFuncSetAttribute(dcn_wgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      return e;
+    KernelScope ks("dcn_wgrad_tc", st);
+    dcn_wgrad_tc_kernel<T><<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  // ---- finalize
+  if (gin) {
+    KernelScope ks("grad_input_to_nchw", st);
+    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
+    nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (goff && (e = convert_f32<T>(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo, st)) != cudaSuccess) return e;
+  if (gmsk && g.use_mask &&
+      (e = convert_f32<T>(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo, st)) != cudaSuccess)
+    return e;
+  if (gw && (e = convert_f32<T>(gw32, gw, (long long)g.Co * g.Cig * g.T, st)) != cudaSuccess) return e;
+  if (gb && (e = convert_f32<T>(gb32, gb, (long long)g.Co, st)) != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+bool tc_backward_supported(const dcn_conv_desc& d, const Geom& g) {
+  return tc_forward_supported(d, g);
+}
+
+size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g) {
+  return bwd_ws(g, 2).total;
+}
+
+cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output, const void* input,
+                        const void* weight, const void* offset, const void* mask, void* grad_input,
+                        void* grad_weight, void* grad_offset, void* grad_mask, void* grad_bias,
+                        void* workspace, cudaStream_t st) {
+  if (d.dtype == DCN_BFLOAT16) {
+    using T = __nv_bfloat16;
+    return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
+                            (const T*)mask, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
+                            (T*)grad_mask, (T*)grad_bias, workspace, st);
+  }
+  using T = __half;
+  return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
+                          (const T*)mask, (T*)grad_input, (T*)grad_weight, (T*)grad_offset, (T*)grad_mask,
+                          (T*)grad_bias, workspace, st);
+}
+
+}  // namespace dcn

@@ -96,3 +96,22 @@ def test_tc_forward_deterministic_and_batch_consistent(cuda):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert torch.equal(a[1:], c)
+
+
+@pytest.mark.parametrize("mask_sel", [(1, 0, 0, 0, 0), (0, 1, 0, 0, 1), (0, 0, 1, 1, 0)])
+def test_tc_backward_output_subsets(mask_sel, cuda):
+    """Only the requested gradients are computed and they match the full call."""
+    import mps_deform_conv as mdc
+    lib = mdc._get_lib()
+    T = _make(SHAPES["c128_g2_og4_dil2"], torch.bfloat16, cuda, seed=5)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    args = (T["grad_output"], T["input"], T["weight"], T["offset"], T["mask"], T["bias"],
+            st[0], st[1], pd[0], pd[1], dl[0], dl[1], 2, 4, True)
+    full = lib.deform_conv2d_backward(*args, [True] * 5)
+    part = lib.deform_conv2d_backward(*args, [bool(v) for v in mask_sel])
+    torch.cuda.synchronize()
+    for f, pz, sel in zip(full, part, mask_sel):
+        if sel:
+            assert rel_err(to_np(pz), to_np(f)) <= 1e-2
+        else:
+            assert pz is None
