@@ -37,11 +37,11 @@ __device__ int g_dcn_status = 0;
 
 namespace {
 
-constexpr int NPROD_WARPS = 8;
-constexpr int NPROD = NPROD_WARPS * 32;
-constexpr int MMA_WARP = 8;
-constexpr int LOAD_WARP = 9;
-constexpr int NTHREADS = 320;
+constexpr int NPROD_WARPS = GATHER_WARPS;
+constexpr int NPROD = GATHER_THREADS;
+constexpr int MMA_WARP = NPROD_WARPS;
+constexpr int LOAD_WARP = NPROD_WARPS + 1;
+constexpr int NTHREADS = (NPROD_WARPS + 2) * 32;
 
 // status codes recorded on a wait that expired
 constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16;
@@ -126,31 +126,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
 
   if (warp < NPROD_WARPS) {
     // ------------------------------------------------ producers
-    const int r = threadIdx.x & (BM - 1);
-    const int v0 = (threadIdx.x >> 7) * 4;
-    const long long pix = (long long)tile * BM + r;
-    const bool valid = pix < g.P;
-    const int b = valid ? (int)(pix / g.HWo) : 0;
-    const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
-    bool ok = true;
-    for (int i = 0; i < a.nkc && ok; ++i) {
-      const int s = i % S;
-      const uint32_t parity = ((i / S) & 1) ^ 1;
-      ok = mbar_wait(empty(s), parity, abort_flag, a.status, ST_PROD);
-      if (!ok) break;
-      const int t = i % g.T, cc = i / g.T;
-      gather_row<T>(g, xh, off, msk, smem + L.a + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
-                    t, grp * g.Cig + cc * BK);
-      fence_async_shared();
-      mbar_arrive(a_full(s));
-    }
+    const int r = warp * 8 + (lane >> 2), cq = lane & 3;
+    const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
+    const bool ok = gather_run<T>(
+        g, xh, off, msk, pc, r, cq, grp * g.Cig, 0, a.nkc, abort_flag, a.status, ST_PROD,
+        [&](int i, uint8_t*& t, uint32_t& eb, uint32_t& par, uint32_t& fb) {
+          const int s = i % S;
+          t = smem + L.a + s * A_STAGE_BYTES;
+          eb = empty(s);
+          par = ((i / S) & 1) ^ 1;
+          fb = a_full(s);
+        });
     // ------------------------------------------------ epilogue
     // (warp-uniform decision: tcgen05.ld is a .sync.aligned warp instruction)
     const bool acc_ready = ok && mbar_wait(acc_full, 0, abort_flag, a.status, ST_EPI);
     if (__all_sync(0xffffffffu, acc_ready)) {
       tc_fence_after();
-      const int q = warp & 3, half = warp >> 2;
-      const int ncol = g.Cog / 2;
+      const int q = warp & 3, quarter = warp >> 2;
       const int row = q * 32 + lane;
       const long long opix = (long long)tile * BM + row;
       const bool ovalid = opix < g.P;
@@ -158,7 +150,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
       const int op = ovalid ? (int)(opix - (long long)ob * g.HWo) : 0;
       T* out = static_cast<T*>(a.out);
       const T* bias = static_cast<const T*>(a.bias);
-      for (int c0 = half * ncol; c0 < (half + 1) * ncol; c0 += 16) {
+      for (int c0 = quarter * 16; c0 < g.Cog; c0 += 64) {
         uint32_t acc[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, acc);
         tmem_ld_wait();
@@ -303,7 +295,7 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   if (d.dtype != DCN_BFLOAT16 && d.dtype != DCN_FLOAT16) return false;
   if (g.Cig % BK != 0) return false;                 // K chunks of 64 channels inside one group
   if (g.cpo % 8 != 0) return false;                  // 16-byte vectors inside one offset group
-  if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N tile: two epilogue halves of x16 loads
+  if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N per MMA: Cog or Cog/2, multiple of 16
   if (pick_stages(g.Cog) < 2) return false;
   return true;
 }

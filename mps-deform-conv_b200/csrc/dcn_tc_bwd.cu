@@ -34,10 +34,10 @@ constexpr int ST_W_PROD = 21, ST_W_MMA = 22, ST_W_LOAD = 23, ST_W_EPI = 24, ST_W
 constexpr int ST_D_MMA = 31, ST_D_LOAD = 32, ST_D_EPI = 33, ST_D_DRAIN = 34;
 
 // ================================================================ wgrad
-constexpr int W_NPROD_WARPS = 8;
-constexpr int W_NPROD = W_NPROD_WARPS * 32;
-constexpr int W_MMA_WARP = 8;
-constexpr int W_NTHREADS = 320;
+constexpr int W_NPROD_WARPS = GATHER_WARPS;
+constexpr int W_NPROD = GATHER_THREADS;
+constexpr int W_MMA_WARP = W_NPROD_WARPS;
+constexpr int W_NTHREADS = (W_NPROD_WARPS + 2) * 32;
 
 struct WgradArgs {
   const void* xh;
@@ -119,33 +119,26 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
 
   if (warp < W_NPROD_WARPS) {
     // -------------------------------------------- col-tile producers
-    const int r = threadIdx.x & (BM - 1);
-    const int v0 = (threadIdx.x >> 7) * 4;
+    const int r = warp * 8 + (lane >> 2), cq = lane & 3;
     bool ok = true;
     for (int li = 0; li < nt && ok; ++li) {
-      const long long pix = (long long)(t0 + li) * BM + r;
-      const bool valid = pix < g.P;
-      const int b = valid ? (int)(pix / g.HWo) : 0;
-      const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
-      for (int kcl = 0; kcl < nk && ok; ++kcl) {
-        const int j = li * nk + kcl;
-        const int s = j % BS;
-        ok = mbar_wait(b_empty(s), ((j / BS) & 1) ^ 1, abort_flag, a.status, ST_W_PROD);
-        if (!ok) break;
-        const int kc = k0 + kcl;
-        const int t = kc % g.T, cc = kc / g.T;
-        gather_row<T>(g, xh, off, msk, smem + L.b + s * A_STAGE_BYTES + r * 128, r, v0, valid, b, p,
-                      t, grp * g.Cig + cc * BK);
-        fence_async_shared();
-        mbar_arrive(b_full(s));
-      }
+      const PixelCtx pc = pixel_ctx(g, (long long)(t0 + li) * BM + r);
+      ok = gather_run<T>(g, xh, off, msk, pc, r, cq, grp * g.Cig, k0, nk, abort_flag, a.status, ST_W_PROD,
+                         [&](int i, uint8_t*& t, uint32_t& eb, uint32_t& par, uint32_t& fb) {
+                           const int j = li * nk + i;
+                           const int s = j % BS;
+                           t = smem + L.b + s * A_STAGE_BYTES;
+                           eb = b_empty(s);
+                           par = ((j / BS) & 1) ^ 1;
+                           fb = b_full(s);
+                         });
     }
     // -------------------------------------------- epilogue: TMEM -> fp32 atomics
     const bool ready = nt > 0 && ok && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
     if (__all_sync(0xffffffffu, ready)) {
       tc_fence_after();
-      const int q = warp & 3, half = warp >> 2;
-      for (int blk = half; blk < a.mh * nk; blk += 2) {
+      const int q = warp & 3, quarter = warp >> 2;
+      for (int blk = quarter; blk < a.mh * nk; blk += W_NPROD_WARPS / 4) {
         const int h = blk / nk, kcl = blk % nk;
         const int co = h * BM + q * 32 + lane;
         const int kc = k0 + kcl;

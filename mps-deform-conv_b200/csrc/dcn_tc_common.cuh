@@ -40,69 +40,166 @@ template <> struct Vec<__half> {
   }
 };
 
-// ---------------------------------------------------------------- producer
-// Gathers one K chunk (tap t, 64 channels starting at c_abs0) of pixel row r
-// for this thread's 4 channel vectors [v0, v0+4) into the swizzled A row.
+// ---------------------------------------------------------------- gather
+// A producer warp owns 8 consecutive pixel rows (8*warp .. 8*warp+7) of a
+// 128-row operand tile [pixels][64 channels].  Lane l works on row
+// 8*warp + l/4 and on the 16-byte channel chunks (l%4) and (l%4)+4 of the
+// K chunk, so one load instruction covers 8 pixels x 64 contiguous bytes of a
+// corner (whole 32-byte sectors).  The offset/mask values of the next K chunk
+// are loaded while the current chunk's corners are in flight.
+constexpr int GATHER_WARPS = 16;
+constexpr int GATHER_THREADS = GATHER_WARPS * 32;
+
+struct PixelCtx {
+  bool valid;
+  int b, p;
+  int y0, x0;       // oy*stride - pad, ox*stride - pad
+  long long img;    // b*H*W (pixel index of the image's first pixel)
+};
+
+__device__ __forceinline__ PixelCtx pixel_ctx(const Geom& g, long long pix) {
+  PixelCtx c;
+  c.valid = pix < g.P;
+  c.b = c.valid ? (int)(pix / g.HWo) : 0;
+  c.p = c.valid ? (int)(pix - (long long)c.b * g.HWo) : 0;
+  const int oy = c.p / g.Wo, ox = c.p - oy * g.Wo;
+  c.y0 = oy * g.sh - g.ph;
+  c.x0 = ox * g.sw - g.pw;
+  c.img = (long long)c.b * g.H * g.W;
+  return c;
+}
+
+// Offset and mask values of one (pixel, offset group, tap), kept in the
+// storage type so that the loads stay in flight until the values are used.
 template <typename T>
-__device__ __forceinline__ void gather_row(const Geom& g, const T* __restrict__ xh,
+struct RawSample {
+  T dy, dx, m;
+};
+
+template <typename T>
+__device__ __forceinline__ RawSample<T> load_raw(const Geom& g, const T* __restrict__ off,
+                                                 const T* __restrict__ msk, const PixelCtx& pc, int o,
+                                                 int t) {
+  RawSample<T> r;
+  const long long ob = ((long long)(pc.b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + pc.p;
+  r.dy = off[ob];
+  r.dx = off[ob + g.HWo];
+  r.m = msk ? msk[((long long)(pc.b * g.OG + o) * g.T + t) * g.HWo + pc.p] : from_f<T>(1.f);
+  return r;
+}
+
+// The four bilinear corners of a sample: element offsets of channel 0 of each
+// corner pixel in the channels-last input, and weights including the mask
+// (zero for invalid corners, samples outside (-1,H)x(-1,W), invalid pixels).
+// Sampling point as in the reference (deform_conv2d_mps.mm:160-168).
+struct CornerSet {
+  long long base[4];
+  float w[4];
+};
+
+template <typename T>
+__device__ __forceinline__ CornerSet corner_set(const Geom& g, const PixelCtx& pc, const RawSample<T>& r,
+                                                int ti, int tj) {
+  CornerSet cs;
+  const float y = (float)(pc.y0 + ti * g.dh) + to_f(r.dy);
+  const float x = (float)(pc.x0 + tj * g.dw) + to_f(r.dx);
+  const Corners c = corners_of(y, x, g.H, g.W);
+  const float m = pc.valid ? to_f(r.m) : 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    cs.w[k] = c.w[k] * m;
+    cs.base[k] = (pc.img + c.idx[k]) * g.C;
+  }
+  return cs;
+}
+
+template <typename T>
+__device__ __forceinline__ void load_corners(const T* __restrict__ xh, const CornerSet& cs, int c_abs,
+                                             uint4 (&v)[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    v[k] = (cs.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(xh + cs.base[k] + c_abs))
+                            : make_uint4(0, 0, 0, 0);
+}
+
+// sum_k w[k] * v[k] over 8 channels, rounded to the 16-bit type.
+template <typename T>
+__device__ __forceinline__ uint4 blend8(const uint4 (&v)[4], const float (&w)[4]) {
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f0 = Vec<T>::unpack((&v[0].x)[e]), f1 = Vec<T>::unpack((&v[1].x)[e]);
+    const float2 f2 = Vec<T>::unpack((&v[2].x)[e]), f3 = Vec<T>::unpack((&v[3].x)[e]);
+    const float lo = w[0] * f0.x + w[1] * f1.x + w[2] * f2.x + w[3] * f3.x;
+    const float hi = w[0] * f0.y + w[1] * f1.y + w[2] * f2.y + w[3] * f3.y;
+    o[e] = Vec<T>::pack(lo, hi);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// K-chunk walker: kc = cc*T + t with t = ti*kw + tj, advanced without division.
+struct KWalk {
+  int t, cc, ti, tj;
+  __device__ __forceinline__ void start(const Geom& g, int kc) {
+    cc = kc / g.T;
+    t = kc - cc * g.T;
+    ti = t / g.kw;
+    tj = t - ti * g.kw;
+  }
+  __device__ __forceinline__ void next(const Geom& g) {
+    ++t;
+    if (++tj == g.kw) { tj = 0; ++ti; }
+    if (t == g.T) { t = 0; ti = 0; tj = 0; ++cc; }
+  }
+};
+
+// One producer thread's share of a run of K chunks for one pixel tile: per
+// chunk it waits for its stage to be free, gathers 2 x 16 bytes of 4 corners,
+// blends, and writes its two 16-byte chunks of row r into the swizzled tile.
+// `stage_of(i)` returns (shared-memory tile base, empty-barrier, parity,
+// full-barrier) for the i-th chunk of the run; returns false if a wait expired.
+template <typename T, class StageFn>
+__device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
-                                           uint8_t* arow, int r, int v0, bool valid, int b, int p,
-                                           int t, int c_abs0) {
-  uint4 vals[4][4];
-  float wts[4][4];
-  int cur_o = -1;
-  float w4[4] = {0.f, 0.f, 0.f, 0.f};
-  long long base4[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    const int c_abs = c_abs0 + (v0 + v) * 8;
-    if (valid) {
-      const int o = c_abs / g.cpo;
-      if (o != cur_o) {
-        cur_o = o;
-        float y, x, m;
-        sample_point(g, off, msk, b, o, t, p, &y, &x, &m);
-        const Corners cs = corners_of(y, x, g.H, g.W);
-        const long long img = (long long)b * g.H * g.W;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          w4[k] = cs.w[k] * m;
-          base4[k] = (img + cs.idx[k]) * g.C;
-        }
+                                           const PixelCtx& pc, int r, int cq, int cbase_grp, int kc0,
+                                           int nk, volatile int* abort_flag, int* status, int code,
+                                           StageFn&& stage_of) {
+  KWalk kw;
+  kw.start(g, kc0);
+  int og0 = (cbase_grp + kw.cc * BK + cq * 8) / g.cpo;
+  int og1 = (cbase_grp + kw.cc * BK + cq * 8 + 32) / g.cpo;
+  RawSample<T> raw0 = load_raw(g, (const T*)off, msk, pc, og0, kw.t);
+  RawSample<T> raw1 = load_raw(g, (const T*)off, msk, pc, og1, kw.t);
+  for (int i = 0; i < nk; ++i) {
+    const CornerSet cs0 = corner_set(g, pc, raw0, kw.ti, kw.tj);
+    const CornerSet cs1 = corner_set(g, pc, raw1, kw.ti, kw.tj);
+    const int c0 = cbase_grp + kw.cc * BK + cq * 8;
+    uint4 v0[4], v1[4];
+    load_corners(xh, cs0, c0, v0);
+    load_corners(xh, cs1, c0 + 32, v1);
+    // prefetch the next chunk's offsets and mask
+    KWalk nx = kw;
+    nx.next(g);
+    if (i + 1 < nk) {
+      if (nx.cc != kw.cc) {
+        og0 = (cbase_grp + nx.cc * BK + cq * 8) / g.cpo;
+        og1 = (cbase_grp + nx.cc * BK + cq * 8 + 32) / g.cpo;
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        wts[v][k] = w4[k];
-        vals[v][k] = (w4[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(xh + base4[k] + c_abs))
-                                    : make_uint4(0, 0, 0, 0);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        wts[v][k] = 0.f;
-        vals[v][k] = make_uint4(0, 0, 0, 0);
-      }
+      raw0 = load_raw(g, off, msk, pc, og0, nx.t);
+      raw1 = load_raw(g, off, msk, pc, og1, nx.t);
     }
+    uint8_t* tile;
+    uint32_t empty_bar, parity, full_bar;
+    stage_of(i, tile, empty_bar, parity, full_bar);
+    if (!mbar_wait(empty_bar, parity, abort_flag, status, code)) return false;
+    uint8_t* row = tile + r * 128;
+    *reinterpret_cast<uint4*>(row + ((cq ^ (r & 7)) << 4)) = blend8<T>(v0, cs0.w);
+    *reinterpret_cast<uint4*>(row + (((cq + 4) ^ (r & 7)) << 4)) = blend8<T>(v1, cs1.w);
+    fence_async_shared();
+    mbar_arrive(full_bar);
+    kw = nx;
   }
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&vals[v][0]);
-    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&vals[v][1]);
-    const uint32_t* q2 = reinterpret_cast<const uint32_t*>(&vals[v][2]);
-    const uint32_t* q3 = reinterpret_cast<const uint32_t*>(&vals[v][3]);
-    uint32_t o4[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f0 = Vec<T>::unpack(q0[e]), f1 = Vec<T>::unpack(q1[e]);
-      const float2 f2 = Vec<T>::unpack(q2[e]), f3 = Vec<T>::unpack(q3[e]);
-      const float lo = wts[v][0] * f0.x + wts[v][1] * f1.x + wts[v][2] * f2.x + wts[v][3] * f3.x;
-      const float hi = wts[v][0] * f0.y + wts[v][1] * f1.y + wts[v][2] * f2.y + wts[v][3] * f3.y;
-      o4[e] = Vec<T>::pack(lo, hi);
-    }
-    const int chunk = v0 + v;
-    uint4* dst = reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4));
-    *dst = make_uint4(o4[0], o4[1], o4[2], o4[3]);
-  }
+  return true;
 }
 
 // ---------------------------------------------------------------- TMA (tensor)
