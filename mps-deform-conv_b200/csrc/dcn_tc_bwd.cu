@@ -245,17 +245,29 @@ struct DgradArgs {
   uint32_t idesc;
 };
 
+// Per-warp epilogue scratch: a 16-channel gcol slab of the warp's 32 rows and
+// the rows' sample table (2 eight-channel segments x 16 words: corner pixel
+// indices, bilinear weights, fy, fx, mask, corner-valid bits, partial sums).
+// Row strides of 20 and 36 words keep the 16-byte accesses aligned and
+// spread over the banks.
+struct DgWarpSmem {
+  float slab[32][20];
+  uint32_t tab[32][36];
+};
+
 // Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
-// streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each.
+// streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each;
+// then the epilogue warps' scratch.
 struct DgradSmem {
-  uint32_t a, b, b_stage, bar, total;
+  uint32_t a, b, b_stage, epi, bar, total;
 };
 __host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages) {
   DgradSmem L;
   L.a = 0;
   L.b = (uint32_t)kb * A_STAGE_BYTES;
   L.b_stage = 8192u;
-  L.bar = L.b + b_stages * L.b_stage;
+  L.epi = L.b + b_stages * L.b_stage;
+  L.bar = L.epi + D_EPI_WARPS * (uint32_t)sizeof(DgWarpSmem);
   L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
   return L;
 }
@@ -306,99 +318,159 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
 
   if (warp < D_EPI_WARPS) {
     // -------------------------------------------- epilogue: col2im + col2im_coord
+    // Two phases per 16-channel slab of a gcol tile:
+    //  (1) row owner (lane = TMEM row = pixel): reads its 16 gcol values from
+    //      TMEM into the warp's slab buffer and, when the offset group changes,
+    //      computes the sample's corners into the warp's table;
+    //  (2) 4 lanes per pixel, 4 channels per lane: corner loads and
+    //      red.global.add.v4.f32 scatters cover whole 32-byte sectors; the
+    //      offset/mask partial sums are reduced across the lane pair and
+    //      returned through the table to the row owner, which adds them to
+    //      global memory once per (pixel, offset group, K chunk).
     const T* xh = static_cast<const T*>(a.xh);
     const T* off = static_cast<const T*>(a.off);
     const T* msk = static_cast<const T*>(a.msk);
     const int e = warp >> 2, q = warp & 3;
-    const int r = q * 32 + lane;
-    const long long pix = (long long)tile * BM + r;
-    const bool valid = pix < g.P;
-    const int b = valid ? (int)(pix / g.HWo) : 0;
-    const int p = valid ? (int)(pix - (long long)b * g.HWo) : 0;
-    const long long img = (long long)b * g.H * g.W;
+    DgWarpSmem* ws = reinterpret_cast<DgWarpSmem*>(smem + L.epi) + warp;
+    const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
+    const int qq = lane & 3, seg = qq >> 1;
     bool ok = true;
     for (int i = e; i < a.nkc; i += D_NBUF) {
       const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
       ok = __all_sync(0xffffffffu, ready);
       if (!ok) break;
       tc_fence_after();
-      const int t = i % g.T, cc = i / g.T;
-      const int cbase = grp * g.Cig + cc * BK;
-      int cur_o = -1;
-      float m = 0.f, fy = 0.f, fx = 0.f;
-      float wb[4] = {0.f, 0.f, 0.f, 0.f};    // bilinear weights (0 outside / invalid)
-      bool cv[4] = {false, false, false, false};  // corner in bounds (coordinate derivative)
-      long long cbase4[4] = {0, 0, 0, 0};
-      float gy = 0.f, gx = 0.f, gm = 0.f;
-      auto flush = [&](int o) {
-        if (o < 0 || !valid) return;
-        const long long ob = ((long long)(b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + p;
-        atomicAdd(a.goff32 + ob, m * gy);
-        atomicAdd(a.goff32 + ob + g.HWo, m * gx);
-        if (g.use_mask) atomicAdd(a.gmsk32 + ((long long)(b * g.OG + o) * g.T + t) * g.HWo + p, gm);
-        gy = gx = gm = 0.f;
+      KWalk kw;
+      kw.start(g, i);
+      const int cbase = grp * g.Cig + kw.cc * BK;
+      int coord_o = -1, acc_o = -1;
+      float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
+      // coordinates of the row owner's sample for offset group coord_o
+      int cidx[4] = {0, 0, 0, 0};
+      float cw[4] = {0.f, 0.f, 0.f, 0.f};
+      float cfy = 0.f, cfx = 0.f, cm = 0.f;
+      uint32_t cvb = 0;
+      auto flush = [&]() {
+        if (acc_o >= 0 && pc.valid) {
+          const long long ob = ((long long)(pc.b * g.OG + acc_o) * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          atomicAdd(a.goff32 + ob, run_gy);
+          atomicAdd(a.goff32 + ob + g.HWo, run_gx);
+          if (g.use_mask)
+            atomicAdd(a.gmsk32 + ((long long)(pc.b * g.OG + acc_o) * g.T + kw.t) * g.HWo + pc.p, run_gm);
+        }
+        run_gy = run_gx = run_gm = 0.f;
       };
 #pragma unroll 1
-      for (int sub = 0; sub < 4; ++sub) {
+      for (int sl = 0; sl < 4; ++sl) {
+        // ---- phase 1: row owner
         uint32_t acc[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64 + sub * 16), acc);
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64 + sl * 16), acc);
         tmem_ld_wait();
-        if (!valid) continue;
+        if (sl == 3) {  // last read of this TMEM buffer: let the MMA reuse it
+          tc_fence_before();
+          mbar_arrive(d_empty(e));
+        }
+        float* srow = ws->slab[lane];
 #pragma unroll
-        for (int v2 = 0; v2 < 2; ++v2) {
-          const int c_abs = cbase + sub * 16 + v2 * 8;
-          const int o = c_abs / g.cpo;
-          if (o != cur_o) {
-            flush(cur_o);
-            cur_o = o;
-            float y, x;
-            sample_point(g, off, msk, b, o, t, p, &y, &x, &m);
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4*>(srow + 4 * k) = make_uint4(acc[4 * k], acc[4 * k + 1], acc[4 * k + 2], acc[4 * k + 3]);
+        int slot_o[2];
+#pragma unroll
+        for (int sg = 0; sg < 2; ++sg) {
+          const int o = (cbase + sl * 16 + sg * 8) / g.cpo;
+          slot_o[sg] = o;
+          if (o != coord_o) {
+            coord_o = o;
+            const RawSample<T> raw = load_raw(g, off, msk, pc, o, kw.t);
+            const float y = (float)(pc.y0 + kw.ti * g.dh) + to_f(raw.dy);
+            const float x = (float)(pc.x0 + kw.tj * g.dw) + to_f(raw.dx);
             const Corners cs = corners_of(y, x, g.H, g.W);
-            const CoordCorners cc4 = coord_corners_of(y, x, g.H, g.W);
-            fy = cc4.fy;
-            fx = cc4.fx;
+            const CoordCorners c4 = coord_corners_of(y, x, g.H, g.W);
+            cm = pc.valid ? to_f(raw.m) : 0.f;
+            cfy = c4.fy;
+            cfx = c4.fx;
+            cvb = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              wb[k] = cs.w[k];
-              cv[k] = cc4.v[k];
-              cbase4[k] = (img + cc4.idx[k]) * g.C;
+              const bool v = pc.valid && c4.v[k];
+              cvb |= (v ? 1u : 0u) << k;
+              cidx[k] = v ? (int)(pc.img + c4.idx[k]) : 0;
+              cw[k] = pc.valid ? cs.w[k] : 0.f;
             }
           }
-          uint4 xv[4];
+          uint32_t* trow = ws->tab[lane] + sg * 16;
+          *reinterpret_cast<uint4*>(trow) = make_uint4(cidx[0], cidx[1], cidx[2], cidx[3]);
+          *reinterpret_cast<uint4*>(trow + 4) = make_uint4(__float_as_uint(cw[0]), __float_as_uint(cw[1]),
+                                                           __float_as_uint(cw[2]), __float_as_uint(cw[3]));
+          *reinterpret_cast<uint4*>(trow + 8) = make_uint4(__float_as_uint(cfy), __float_as_uint(cfx),
+                                                           __float_as_uint(cm), cvb);
+        }
+        __syncwarp();
+        // ---- phase 2: 4 lanes per pixel
+#pragma unroll 1
+        for (int it = 0; it < 4; ++it) {
+          const int rr = it * 8 + (lane >> 2);
+          const uint32_t* tr = ws->tab[rr] + seg * 16;
+          const uint4 tb = *reinterpret_cast<const uint4*>(tr);
+          const uint4 tw = *reinterpret_cast<const uint4*>(tr + 4);
+          const uint4 tx = *reinterpret_cast<const uint4*>(tr + 8);
+          const float4 gv = *reinterpret_cast<const float4*>(ws->slab[rr] + qq * 4);
+          const int c_abs = cbase + sl * 16 + qq * 4;
+          const int ci[4] = {(int)tb.x, (int)tb.y, (int)tb.z, (int)tb.w};
+          const float w[4] = {__uint_as_float(tw.x), __uint_as_float(tw.y), __uint_as_float(tw.z),
+                              __uint_as_float(tw.w)};
+          const float fy = __uint_as_float(tx.x), fx = __uint_as_float(tx.y), m = __uint_as_float(tx.z);
+          const uint32_t cv = tx.w;
+          uint2 xv[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            xv[k] = cv[k] ? __ldg(reinterpret_cast<const uint4*>(xh + cbase4[k] + c_abs)) : make_uint4(0, 0, 0, 0);
-          float gv[8];
+            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + (long long)ci[k] * g.C + c_abs))
+                                   : make_uint2(0, 0);
+          const float gvv[4] = {gv.x, gv.y, gv.z, gv.w};
+          float pgy = 0.f, pgx = 0.f, pgm = 0.f;
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) gv[jj] = __uint_as_float(acc[v2 * 8 + jj]);
-#pragma unroll
-          for (int w2 = 0; w2 < 4; ++w2) {
-            const float2 f0 = Vec<T>::unpack((&xv[0].x)[w2]);
-            const float2 f1 = Vec<T>::unpack((&xv[1].x)[w2]);
-            const float2 f2 = Vec<T>::unpack((&xv[2].x)[w2]);
-            const float2 f3 = Vec<T>::unpack((&xv[3].x)[w2]);
-            const float ga = gv[2 * w2], gb = gv[2 * w2 + 1];
-            gm += ga * (wb[0] * f0.x + wb[1] * f1.x + wb[2] * f2.x + wb[3] * f3.x);
-            gm += gb * (wb[0] * f0.y + wb[1] * f1.y + wb[2] * f2.y + wb[3] * f3.y);
-            gy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
-            gy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
-            gx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
-            gx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
+          for (int h = 0; h < 2; ++h) {
+            const float2 f0 = Vec<T>::unpack((&xv[0].x)[h]), f1 = Vec<T>::unpack((&xv[1].x)[h]);
+            const float2 f2 = Vec<T>::unpack((&xv[2].x)[h]), f3 = Vec<T>::unpack((&xv[3].x)[h]);
+            const float ga = gvv[2 * h], gb = gvv[2 * h + 1];
+            pgm += ga * (w[0] * f0.x + w[1] * f1.x + w[2] * f2.x + w[3] * f3.x);
+            pgm += gb * (w[0] * f0.y + w[1] * f1.y + w[2] * f2.y + w[3] * f3.y);
+            pgy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
+            pgy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
+            pgx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
+            pgx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const float wk = wb[k] * m;
-            if (wk != 0.f) {
-              float* dst = a.gi32 + cbase4[k] + c_abs;
-              red_v4(dst, wk * gv[0], wk * gv[1], wk * gv[2], wk * gv[3]);
-              red_v4(dst + 4, wk * gv[4], wk * gv[5], wk * gv[6], wk * gv[7]);
-            }
+            const float wk = w[k] * m;
+            if (wk != 0.f)
+              red_v4(a.gi32 + (long long)ci[k] * g.C + c_abs, wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
+          }
+          pgy += __shfl_xor_sync(0xffffffffu, pgy, 1);
+          pgx += __shfl_xor_sync(0xffffffffu, pgx, 1);
+          pgm += __shfl_xor_sync(0xffffffffu, pgm, 1);
+          if ((qq & 1) == 0) {
+            uint32_t* tw2 = ws->tab[rr] + seg * 16 + 12;
+            *reinterpret_cast<uint4*>(tw2) = make_uint4(__float_as_uint(m * pgy), __float_as_uint(m * pgx),
+                                                        __float_as_uint(pgm), 0u);
           }
         }
+        __syncwarp();
+        // ---- row owner collects this slab's partial sums
+#pragma unroll
+        for (int sg = 0; sg < 2; ++sg) {
+          if (slot_o[sg] != acc_o) {
+            flush();
+            acc_o = slot_o[sg];
+          }
+          const uint4 pa = *reinterpret_cast<const uint4*>(ws->tab[lane] + sg * 16 + 12);
+          run_gy += __uint_as_float(pa.x);
+          run_gx += __uint_as_float(pa.y);
+          run_gm += __uint_as_float(pa.z);
+        }
+        __syncwarp();
       }
-      flush(cur_o);
-      tc_fence_before();
-      mbar_arrive(d_empty(e));
+      flush();
     }
   } else if (warp == D_MMA_WARP) {
     // -------------------------------------------- MMA issuer
@@ -637,7 +709,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.wdt = wdt;
     a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
     a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
-    a.b_stages = 8;
+    a.b_stages = 4;
     while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) --a.b_stages;
     if (dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
     a.idesc = idesc_f16(BM, 64, bf16);
@@ -700,7 +772,9 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
 }  // namespace
 
 bool tc_backward_supported(const dcn_conv_desc& d, const Geom& g) {
-  return tc_forward_supported(d, g);
+  // dgrad keeps the [128 px][C_out/group] grad_output tile resident next to
+  // the epilogue scratch: C_out/group <= 256; corner indices are 32-bit.
+  return tc_forward_supported(d, g) && g.Cog <= 256 && (long long)g.B * g.H * g.W < (1LL << 31);
 }
 
 size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g) {
