@@ -31,6 +31,7 @@ sys.path.insert(0, REPO)
 
 import torch  # noqa: E402
 
+from mps_deform_conv.sharding import allreduce_param_grads, shard_range  # noqa: E402
 from mps_deform_conv.workloads import PROBLEMS, make_inputs  # noqa: E402
 
 METRIC = "deform_conv2d fwd+bwd TFLOP/s & % roofline per B200; samples/s at 1/2/4/8 GPUs"
@@ -206,10 +207,9 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     p = PROBLEMS[args.workload]
-    assert p.batch % world == 0, f"global batch {p.batch} not divisible by {world} ranks"
-    nb = p.batch // world
+    first, nb = shard_range(p.batch, world, rank)
     peaks = load_peaks()
-    inp = make_inputs(p, dev, batch=nb, batch_offset=rank * nb)
+    inp = make_inputs(p, dev, batch=nb, batch_offset=first)
     stride, pad, dil = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
     x, off, w, b, m, go = (inp[k] for k in ("input", "offset", "weight", "bias", "mask", "grad_output"))
     leaves = [t for t in (x, off, w, b, m) if t is not None]
@@ -218,17 +218,9 @@ def run_ours(args):
             t.requires_grad_(True)
     param_grads_idx = [2] + ([3] if b is not None else [])
 
-    def allreduce_param_grads(grads):
-        if world == 1:
-            return
-        import torch.distributed as dist
-        pg = [grads[i] for i in range(len(grads)) if leaves[i] is w or leaves[i] is b]
-        flat = torch.cat([g.reshape(-1) for g in pg])
-        dist.all_reduce(flat)
-        o = 0
-        for g in pg:
-            g.copy_(flat[o:o + g.numel()].view_as(g))
-            o += g.numel()
+    def reduce_grads(grads):
+        if world > 1:  # grad_weight and grad_bias sum over the global batch
+            allreduce_param_grads([grads[i] for i in range(len(grads)) if leaves[i] is w or leaves[i] is b])
 
     fwd_ev = []
 
@@ -238,7 +230,7 @@ def run_ours(args):
             record.record()
         if p.training:
             grads = torch.autograd.grad(out, leaves, go)
-            allreduce_param_grads(grads)
+            reduce_grads(grads)
             return grads
         return out
 
@@ -302,7 +294,7 @@ def run_ours(args):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(p, inp, args, dev, world, allreduce_param_grads, leaves)
+        e2e = run_e2e(p, inp, args, dev, world)
 
     # ---- CPU baseline on rank 0 at N=1
     cpu = None
@@ -318,7 +310,8 @@ def run_ours(args):
             "dtype": {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[p.dtype],
             "data": "synthetic (seeded; workload distributions)",
             "config": {"workload": p.name, "description": p.description, "global_batch": p.batch,
-                       "per_gpu_batch": nb, "parallelism": f"batch-sharded dp{world}",
+                       "per_gpu_batch": nb, "parallelism": f"batch-sharded dp{world}" + (
+                           ", grad_weight/grad_bias NCCL all-reduce" if world > 1 and p.training else ""),
                        "l2": "flushed between steps (256 MB write)" if flush is not None
                        else f"inputs {in_bytes / 2**20:.0f} MB per rank > L2",
                        "fwd_ms_per_step": round(sum(fwd_ms) / args.steps, 4)},
@@ -356,7 +349,7 @@ def kernel_roofline(p, nb, name):
     return {"bound": "hbm", "per_launch": x + off + msk, "note": "input+offset+mask bytes"}
 
 
-def run_e2e(p, inp, args, dev, world, allreduce_param_grads, leaves):
+def run_e2e(p, inp, args, dev, world):
     """Same step through the public API, inputs copied from pinned host memory
     every step and the parameter gradients read back to the host."""
     import mps_deform_conv as mdc
@@ -382,12 +375,7 @@ def run_e2e(p, inp, args, dev, world, allreduce_param_grads, leaves):
             gw = grads[2]
             gb = grads[3] if dev_b is not None else None
             if world > 1:
-                import torch.distributed as dist
-                flat = torch.cat([gw.reshape(-1)] + ([gb.reshape(-1)] if gb is not None else []))
-                dist.all_reduce(flat)
-                gw = flat[:gw.numel()].view_as(gw)
-                if gb is not None:
-                    gb = flat[gw.numel():]
+                allreduce_param_grads([gw, gb])
             out_host.copy_(gw, non_blocking=True)
             if gb is not None:
                 outb_host.copy_(gb, non_blocking=True)

@@ -1,0 +1,52 @@
+"""Batch sharding across ranks for deformable-convolution layers.
+
+Samples are independent in the forward pass and in grad_input / grad_offset /
+grad_mask, so a global batch splits across ranks with no exchange; only the
+parameter gradients (grad_weight, grad_bias) sum over the batch.  This module
+holds the two host-side pieces of that scheme:
+
+* ``shard_range`` -- which contiguous samples of the global batch a rank owns;
+* ``allreduce_param_grads`` -- one all-reduce (sum) of the parameter gradients
+  packed into a single flat bucket, so a step issues one collective instead of
+  one per tensor.  Works on any torch.distributed backend (NCCL over NVLink on
+  GPUs, gloo on CPU).
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+
+def shard_range(global_batch: int, world_size: int, rank: int) -> Tuple[int, int]:
+    """(first sample, sample count) of `rank`'s shard; shards differ by at most one sample."""
+    if world_size <= 0 or not (0 <= rank < world_size):
+        raise ValueError(f"invalid rank {rank} for world size {world_size}")
+    base, extra = divmod(global_batch, world_size)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def allreduce_param_grads(grads: Sequence[Optional[torch.Tensor]], group=None,
+                          average: bool = False) -> List[Optional[torch.Tensor]]:
+    """Sum (or average) the given gradients over all ranks in one flat-bucket all-reduce.
+
+    The gradients are packed into one contiguous buffer of their common dtype,
+    reduced in place, and copied back into the original tensors, which are
+    returned.  ``None`` entries are passed through.
+    """
+    import torch.distributed as dist
+
+    present = [g for g in grads if g is not None]
+    if not present or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return list(grads)
+    flat = torch.cat([g.reshape(-1) for g in present])
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    if average:
+        flat /= dist.get_world_size(group)
+    off = 0
+    for g in present:
+        n = g.numel()
+        g.copy_(flat[off:off + n].view_as(g))
+        off += n
+    return list(grads)
