@@ -182,6 +182,34 @@ DCN_API int dcn_deform_conv2d_backward(const dcn_conv_desc *desc, const void *gr
                                void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------
+ * Training pair.  The forward can leave state resident on the device for
+ * the backward of the same call: a channels-last copy of the input and the
+ * gathered column tiles of the forward's GEMM (the reference builds the
+ * column buffer in its forward and rebuilds it in its backward,
+ * deform_conv2d_mps.mm:679-758 and mps_deform_conv/__init__.py:266-273).
+ * With it the backward skips the input re-layout and the column re-gather:
+ * the weight-gradient GEMM streams the saved tiles.  The state costs
+ * dcn_saved_state_bytes() of device memory (about B*Ho*Wo*C*kh*kw*2 bytes)
+ * between the two calls; 0 means this problem keeps nothing (SIMT kernels),
+ * and the _train calls then behave like the plain ones.  `saved` must not be
+ * modified between the forward and the backward.
+ */
+DCN_API size_t dcn_saved_state_bytes(const dcn_conv_desc *desc);
+DCN_API int dcn_deform_conv2d_forward_train(const dcn_conv_desc *desc, const void *input,
+                                            const void *weight, const void *offset,
+                                            const void *mask, const void *bias, void *output,
+                                            void *saved, size_t saved_bytes, void *workspace,
+                                            size_t workspace_bytes, void *stream);
+DCN_API int dcn_deform_conv2d_backward_train(const dcn_conv_desc *desc, const void *grad_output,
+                                             const void *input, const void *weight,
+                                             const void *offset, const void *mask,
+                                             const void *saved, size_t saved_bytes,
+                                             void *grad_input, void *grad_weight,
+                                             void *grad_offset, void *grad_mask, void *grad_bias,
+                                             void *workspace, size_t workspace_bytes,
+                                             void *stream);
+
+/* ---------------------------------------------------------------------
  * Device status.  Kernels with bounded waits record an expired wait in a
  * device-side status word instead of hanging.  This call copies and clears
  * it (it synchronises `stream`): DCN_OK, or DCN_ERR_DEVICE_TIMEOUT.

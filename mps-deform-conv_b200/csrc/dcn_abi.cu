@@ -266,9 +266,10 @@ size_t dcn_forward_workspace_size(const dcn_conv_desc* d) {
   return tc_forward_supported(*d, g) ? tc_forward_workspace(*d, g) : 0;
 }
 
-int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const void* weight,
-                              const void* offset, const void* mask, const void* bias, void* output,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+static int forward_impl(const dcn_conv_desc* d, const void* input, const void* weight,
+                        const void* offset, const void* mask, const void* bias, void* output,
+                        void* saved, size_t saved_bytes, void* workspace, size_t workspace_bytes,
+                        void* stream) {
   int r = validate(d);
   if (r != DCN_OK) return r;
   const Geom g = make_geom(*d);
@@ -282,7 +283,10 @@ int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const v
     if (workspace_bytes < need || (need && !workspace))
       return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need,
                   workspace_bytes);
-    cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, st);
+    const size_t need_saved = saved ? saved_layout(g).total : 0;
+    if (saved && saved_bytes < need_saved)
+      return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", need_saved, saved_bytes);
+    cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, saved, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward (tensor core)");
   }
   cudaError_t e = cudaSuccess;
@@ -293,6 +297,29 @@ int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const v
     return 0;
   });
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward");
+}
+
+int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const void* weight,
+                              const void* offset, const void* mask, const void* bias, void* output,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(d, input, weight, offset, mask, bias, output, nullptr, 0, workspace,
+                      workspace_bytes, stream);
+}
+
+size_t dcn_saved_state_bytes(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK) return 0;
+  const Geom g = make_geom(*d);
+  return tc_backward_supported(*d, g) ? saved_layout(g).total : 0;
+}
+
+int dcn_deform_conv2d_forward_train(const dcn_conv_desc* d, const void* input, const void* weight,
+                                    const void* offset, const void* mask, const void* bias,
+                                    void* output, void* saved, size_t saved_bytes, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (validate(d) != DCN_OK) return validate(d);
+  if (dcn_saved_state_bytes(d) == 0) saved = nullptr;
+  return forward_impl(d, input, weight, offset, mask, bias, output, saved, saved_bytes, workspace,
+                      workspace_bytes, stream);
 }
 
 int dcn_deformable_im2col(const dcn_conv_desc* d0, const void* input, const void* offset,
@@ -381,11 +408,11 @@ size_t dcn_backward_workspace_size(const dcn_conv_desc* d) {
   return simt_bwd_layout(d, g).total;
 }
 
-int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, const void* input,
-                               const void* weight, const void* offset, const void* mask,
-                               void* grad_input, void* grad_weight, void* grad_offset,
-                               void* grad_mask, void* grad_bias, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const void* input,
+                         const void* weight, const void* offset, const void* mask,
+                         const void* saved, size_t saved_bytes, void* grad_input,
+                         void* grad_weight, void* grad_offset, void* grad_mask, void* grad_bias,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   int r = validate(d);
   if (r != DCN_OK) return r;
   const Geom g = make_geom(*d);
@@ -406,8 +433,11 @@ int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, 
     if (workspace_bytes < need || (need && !workspace))
       return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,
                   workspace_bytes);
-    cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset, mask, grad_input, grad_weight,
-                                grad_offset, grad_mask, grad_bias, workspace, st);
+    if (saved && saved_bytes < saved_layout(g).total)
+      return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
+                  saved_bytes);
+    cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset, mask, saved, grad_input,
+                                grad_weight, grad_offset, grad_mask, grad_bias, workspace, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward (tensor core)");
   }
   const SimtBwdLayout L = simt_bwd_layout(d, g);
@@ -430,6 +460,28 @@ int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, 
     return 0;
   });
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
+}
+
+int dcn_deform_conv2d_backward(const dcn_conv_desc* d, const void* grad_output, const void* input,
+                               const void* weight, const void* offset, const void* mask,
+                               void* grad_input, void* grad_weight, void* grad_offset,
+                               void* grad_mask, void* grad_bias, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return backward_impl(d, grad_output, input, weight, offset, mask, nullptr, 0, grad_input, grad_weight,
+                       grad_offset, grad_mask, grad_bias, workspace, workspace_bytes, stream);
+}
+
+int dcn_deform_conv2d_backward_train(const dcn_conv_desc* d, const void* grad_output,
+                                     const void* input, const void* weight, const void* offset,
+                                     const void* mask, const void* saved, size_t saved_bytes,
+                                     void* grad_input, void* grad_weight, void* grad_offset,
+                                     void* grad_mask, void* grad_bias, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (validate(d) != DCN_OK) return validate(d);
+  if (dcn_saved_state_bytes(d) == 0) saved = nullptr;
+  return backward_impl(d, grad_output, input, weight, offset, mask, saved, saved_bytes, grad_input,
+                       grad_weight, grad_offset, grad_mask, grad_bias, workspace, workspace_bytes,
+                       stream);
 }
 
 int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void* grad_col,

@@ -71,6 +71,7 @@ struct FwdArgs {
   const void* bias;   // [Co] or null
   void* out;          // [B][Co][Ho][Wo]
   const void* wsw;    // weights, pre-swizzled [G][NKC][Cog][64]
+  void* cols;         // copy of every A tile [G][n_tiles][NKC][16 KB], or null
   int* status;
   Geom g;
   int nkc;            // K chunks per group = (Cig / 64) * T
@@ -130,9 +131,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
     const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
     const bool ok = gather_run<T>(
         g, xh, off, msk, pc, r, cq, grp * g.Cig, 0, a.nkc, abort_flag, a.status, ST_PROD,
-        [&](int i, uint8_t*& t, uint32_t& eb, uint32_t& par, uint32_t& fb) {
+        [&](int i, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& par, uint32_t& fb) {
           const int s = i % S;
           t = smem + L.a + s * A_STAGE_BYTES;
+          gt = a.cols ? static_cast<uint8_t*>(a.cols) +
+                            (((size_t)grp * gridDim.x + tile) * a.nkc + i) * (size_t)A_STAGE_BYTES
+                      : nullptr;
           eb = empty(s);
           par = ((i / S) & 1) ^ 1;
           fb = a_full(s);
@@ -315,6 +319,16 @@ size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g) {
   return fwd_ws(g, 2).total;
 }
 
+SavedLayout saved_layout(const Geom& g) {
+  SavedLayout L;
+  const size_t n_tiles = (size_t)((g.P + BM - 1) / BM);
+  const size_t nkc = (size_t)(g.Cig / BK) * g.T;
+  L.xh = 0;
+  L.cols = ws_align(2 * (size_t)g.B * g.H * g.W * g.C);
+  L.total = L.cols + ws_align((size_t)g.G * n_tiles * nkc * A_STAGE_BYTES);
+  return L;
+}
+
 int* tc_status_ptr() {
   static int* p = nullptr;  // one device address per process (first device that asks)
   if (!p) {
@@ -351,9 +365,11 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, 
 
 template <typename T>
 static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
-                                const T* bias, T* out, void* workspace, cudaStream_t st) {
+                                const T* bias, T* out, void* workspace, void* saved, cudaStream_t st) {
   const FwdWs L = fwd_ws(g, sizeof(T));
-  T* xh = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.xh);
+  const SavedLayout SV = saved_layout(g);
+  T* xh = reinterpret_cast<T*>(saved ? static_cast<char*>(saved) + SV.xh
+                                     : static_cast<char*>(workspace) + L.xh);
   T* wsw = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.wsw);
   cudaError_t e;
   {
@@ -373,6 +389,7 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
 
   FwdArgs a;
   a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.bias = bias; a.out = out; a.wsw = wsw;
+  a.cols = saved ? static_cast<char*>(saved) + SV.cols : nullptr;
   a.status = tc_status_ptr();
   if (!a.status) return cudaErrorSymbolNotFound;
   a.g = g;
@@ -396,13 +413,15 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
 
 cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
                        const void* offset, const void* mask, const void* bias, void* output,
-                       void* workspace, cudaStream_t st) {
+                       void* workspace, void* saved, cudaStream_t st) {
   if (d.dtype == DCN_BFLOAT16)
     return tc_forward_t<__nv_bfloat16>(g, (const __nv_bfloat16*)input, (const __nv_bfloat16*)weight,
                                        (const __nv_bfloat16*)offset, (const __nv_bfloat16*)mask,
-                                       (const __nv_bfloat16*)bias, (__nv_bfloat16*)output, workspace, st);
+                                       (const __nv_bfloat16*)bias, (__nv_bfloat16*)output, workspace,
+                                       saved, st);
   return tc_forward_t<__half>(g, (const __half*)input, (const __half*)weight, (const __half*)offset,
-                              (const __half*)mask, (const __half*)bias, (__half*)output, workspace, st);
+                              (const __half*)mask, (const __half*)bias, (__half*)output, workspace,
+                              saved, st);
 }
 
 

@@ -12,13 +12,26 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g);
 bool tc_backward_supported(const dcn_conv_desc& d, const Geom& g);
 size_t tc_forward_workspace(const dcn_conv_desc& d, const Geom& g);
 size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g);
+
+// Training state the forward can leave resident for the backward:
+//   xh    channels-last copy of the input [B][H][W][C]
+//   cols  the forward's gathered A-operand tiles [G][n_tiles][NKC][16 KB],
+//         each tile [128 pixels][64 channels] in the 128-byte-swizzled
+//         shared-memory image, so the weight-gradient GEMM streams them back
+//         with bulk copies instead of gathering again.
+struct SavedLayout {
+  size_t xh, cols, total;
+};
+SavedLayout saved_layout(const Geom& g);
+
+// `saved` may be null (nothing kept / nothing available).
 cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
                        const void* offset, const void* mask, const void* bias, void* output,
-                       void* workspace, cudaStream_t st);
+                       void* workspace, void* saved, cudaStream_t st);
 cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output,
                         const void* input, const void* weight, const void* offset, const void* mask,
-                        void* grad_input, void* grad_weight, void* grad_offset, void* grad_mask,
-                        void* grad_bias, void* workspace, cudaStream_t st);
+                        const void* saved, void* grad_input, void* grad_weight, void* grad_offset,
+                        void* grad_mask, void* grad_bias, void* workspace, cudaStream_t st);
 // Copies the device status word (non-zero after an expired bounded wait)
 // into *out and clears it; synchronises the stream.
 cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st);

@@ -124,10 +124,11 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
     for (int li = 0; li < nt && ok; ++li) {
       const PixelCtx pc = pixel_ctx(g, (long long)(t0 + li) * BM + r);
       ok = gather_run<T>(g, xh, off, msk, pc, r, cq, grp * g.Cig, k0, nk, abort_flag, a.status, ST_W_PROD,
-                         [&](int i, uint8_t*& t, uint32_t& eb, uint32_t& par, uint32_t& fb) {
+                         [&](int i, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& par, uint32_t& fb) {
                            const int j = li * nk + i;
                            const int s = j % BS;
                            t = smem + L.b + s * A_STAGE_BYTES;
+                           gt = nullptr;
                            eb = b_empty(s);
                            par = ((j / BS) & 1) ^ 1;
                            fb = b_full(s);
@@ -217,6 +218,163 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
   tc_fence_before();
   __syncthreads();
   if (warp == W_MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------- wgrad from saved columns
+// Same GEMM as dcn_wgrad_tc_kernel, but the column tiles are the forward's
+// (saved in their shared-memory image) and arrive by bulk copy: no gather.
+// Warps 0-3 epilogue, warp 4 MMA, warp 5 loader (gOt by TMA + column tiles).
+constexpr int WC_EPI_WARPS = 4;
+constexpr int WC_MMA_WARP = 4;
+constexpr int WC_NTHREADS = 192;
+
+template <typename T>
+__global__ void __launch_bounds__(WC_NTHREADS, 1)
+dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
+                         const __grid_constant__ CUtensorMap tmap_go) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Geom& g = a.g;
+  const int AS = a.a_stages, BS = a.b_stages;
+  const WgradSmem L = wgrad_smem(a.mh, AS, BS);
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + L.bar;
+  auto a_full = [&](int s) { return bar0 + 8u * s; };
+  auto a_empty = [&](int s) { return bar0 + 8u * (AS + s); };
+  auto b_full = [&](int s) { return bar0 + 8u * (2 * AS + s); };
+  auto b_empty = [&](int s) { return bar0 + 8u * (2 * AS + BS + s); };
+  const uint32_t d_full = bar0 + 8u * (2 * AS + 2 * BS);
+  const uint32_t drain = d_full + 8u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (2 * AS + 2 * BS + 2) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = blockIdx.y;
+  const int k0 = blockIdx.x * a.nkg;
+  const int nk = min(a.nkg, a.nkc - k0);
+  const int t0 = blockIdx.z * a.tiles_per_cta;
+  const int nt = max(0, min(a.tiles_per_cta, a.n_tiles - t0));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AS; ++s) { mbar_init(a_full(s), 1); mbar_init(a_empty(s), 1); }
+    for (int s = 0; s < BS; ++s) { mbar_init(b_full(s), 1); mbar_init(b_empty(s), 1); }
+    mbar_init(d_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WC_MMA_WARP) {
+    tmem_alloc(smem_addr(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < WC_EPI_WARPS) {
+    // -------------------------------------------- epilogue: TMEM -> fp32 atomics
+    const bool ready = nt > 0 && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
+    if (__all_sync(0xffffffffu, ready)) {
+      tc_fence_after();
+      const int q = warp;
+      for (int blk = 0; blk < a.mh * nk; ++blk) {
+        const int h = blk / nk, kcl = blk % nk;
+        const int co = h * BM + q * 32 + lane;
+        const int kc = k0 + kcl;
+        const int t = kc % g.T, cc = kc / g.T;
+        const uint32_t col = (uint32_t)((h * a.nkg + kcl) * 64);
+#pragma unroll 1
+        for (int c16 = 0; c16 < 4; ++c16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + col + c16 * 16, v);
+          tmem_ld_wait();
+          if (co < g.Cog) {
+            float* dst = a.gw32 + ((long long)(grp * g.Cog + co) * g.Cig + cc * BK + c16 * 16) * g.T + t;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) atomicAdd(dst + (long long)jj * g.T, __uint_as_float(v[jj]));
+          }
+        }
+      }
+    }
+  } else if (warp == WC_MMA_WARP) {
+    // -------------------------------------------- MMA issuer
+    if (lane == 0 && nt > 0) {
+      bool ok = true;
+      int committed = 0;
+      for (int li = 0; li < nt && ok; ++li) {
+        const int as = li % AS;
+        ok = mbar_wait(a_full(as), (li / AS) & 1, abort_flag, a.status, ST_W_MMA);
+        if (!ok) break;
+        const uint32_t abase = sbase + L.a + as * L.a_stage;
+        for (int kcl = 0; kcl < nk && ok; ++kcl) {
+          const int j = li * nk + kcl;
+          const int s = j % BS;
+          ok = mbar_wait(b_full(s), (j / BS) & 1, abort_flag, a.status, ST_W_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t bbase = sbase + L.b + s * A_STAGE_BYTES;
+          for (int h = 0; h < a.mh; ++h) {
+            const uint32_t dcol = (uint32_t)((h * a.nkg + kcl) * 64);
+#pragma unroll
+            for (int kk = 0; kk < BM / 16; ++kk) {
+              const uint64_t ad = desc_mnmajor_sw128(abase + h * 2 * A_STAGE_BYTES + kk * 2048, A_STAGE_BYTES);
+              const uint64_t bd = desc_mnmajor_sw128(bbase + kk * 2048, A_STAGE_BYTES);
+              mma_f16(tmem + dcol, ad, bd, a.idesc, (li > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(b_empty(s));
+          ++committed;
+        }
+        if (ok) mma_commit(a_empty(as));
+      }
+      if (ok) {
+        mma_commit(d_full);
+      } else if (committed > 0) {
+        mma_commit(drain);
+        mbar_wait(drain, 0, abort_flag, a.status, ST_W_DRAIN);
+      }
+    }
+  } else {
+    // -------------------------------------------- loader: gOt tiles (TMA) + column tiles (bulk)
+    if (lane == 0 && nt > 0) {
+      const uint32_t abytes = (uint32_t)a.ncb * A_STAGE_BYTES;
+      int a_issued = 0, b_issued = 0;
+      bool ok = true;
+      for (int li = 0; li < nt && ok; ++li) {
+        const int as = li % AS;
+        ok = mbar_wait(a_empty(as), ((li / AS) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD);
+        if (!ok) break;
+        mbar_arrive_expect_tx(a_full(as), abytes);
+        const uint32_t dst = sbase + L.a + as * L.a_stage;
+        for (int cb = 0; cb < a.ncb; ++cb)
+          tma_load_2d(dst + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, (t0 + li) * BM, a_full(as));
+        ++a_issued;
+        const uint8_t* src = static_cast<const uint8_t*>(cols) +
+                             (((size_t)grp * a.n_tiles + t0 + li) * a.nkc + k0) * (size_t)A_STAGE_BYTES;
+        for (int kcl = 0; kcl < nk; ++kcl) {
+          const int j = li * nk + kcl;
+          const int s = j % BS;
+          ok = mbar_wait(b_empty(s), ((j / BS) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD);
+          if (!ok) break;
+          mbar_arrive_expect_tx(b_full(s), A_STAGE_BYTES);
+          bulk_g2s(sbase + L.b + s * A_STAGE_BYTES, src + (size_t)kcl * A_STAGE_BYTES, A_STAGE_BYTES, b_full(s));
+          ++b_issued;
+        }
+      }
+      for (int li = (a_issued > AS ? a_issued - AS : 0); li < a_issued; ++li)
+        mbar_wait(a_full(li % AS), (li / AS) & 1, abort_flag, a.status, ST_W_LOAD);
+      for (int j = (b_issued > BS ? b_issued - BS : 0); j < b_issued; ++j)
+        mbar_wait(b_full(j % BS), (j / BS) & 1, abort_flag, a.status, ST_W_LOAD);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == WC_MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
   }
@@ -661,11 +819,15 @@ static int grid_cap(long long n) {
 
 template <typename T>
 cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, const T* off, const T* msk,
-                          T* gin, T* gw, T* goff, T* gmsk, T* gb, void* workspace, cudaStream_t st) {
+                          const void* saved, T* gin, T* gw, T* goff, T* gmsk, T* gb, void* workspace,
+                          cudaStream_t st) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const BwdWs L = bwd_ws(g, sizeof(T));
   char* ws = static_cast<char*>(workspace);
-  T* xh = reinterpret_cast<T*>(ws + L.xh);
+  const SavedLayout SV = saved_layout(g);
+  T* xh = saved ? reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.xh)
+                : reinterpret_cast<T*>(ws + L.xh);
+  const void* cols = saved ? static_cast<const char*>(saved) + SV.cols : nullptr;
   T* got = reinterpret_cast<T*>(ws + L.got);
   T* wdt = reinterpret_cast<T*>(ws + L.wdt);
   float* gi32 = reinterpret_cast<float*>(ws + L.gi32);
@@ -688,7 +850,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     go_transpose_bias_kernel<T><<<grid, 256, 0, st>>>(go, got, gb ? gb32 : nullptr, g.Co, g.HWo);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  {
+  if (!saved) {  // channels-last input copy, unless the forward left one
     KernelScope ks("nchw_to_nhwc", st);
     dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
     nchw_to_nhwc_bwd_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
@@ -747,10 +909,18 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.idesc = idesc_f16_major(BM, 64, bf16, true, true);
     a.tmem_cols = pow2_cols(a.mh * a.nkg * 64);
     const int smem = (int)wgrad_smem(a.mh, a.a_stages, a.b_stages).total + 1024;
-    if ((e = cudaFuncSetAttribute(dcn_wgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
-      return e;
-    KernelScope ks("dcn_wgrad_tc", st);
-    dcn_wgrad_tc_kernel<T><<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
+    if (cols) {
+      if ((e = cudaFuncSetAttribute(dcn_wgrad_cols_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    smem)) != cudaSuccess)
+        return e;
+      KernelScope ks("dcn_wgrad_cols_tc", st);
+      dcn_wgrad_cols_tc_kernel<T><<<dim3(kgroups, g.G, splits), WC_NTHREADS, smem, st>>>(a, cols, tmap);
+    } else {
+      if ((e = cudaFuncSetAttribute(dcn_wgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+        return e;
+      KernelScope ks("dcn_wgrad_tc", st);
+      dcn_wgrad_tc_kernel<T><<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   // ---- finalize
@@ -782,19 +952,19 @@ size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g) {
 }
 
 cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output, const void* input,
-                        const void* weight, const void* offset, const void* mask, void* grad_input,
-                        void* grad_weight, void* grad_offset, void* grad_mask, void* grad_bias,
-                        void* workspace, cudaStream_t st) {
+                        const void* weight, const void* offset, const void* mask, const void* saved,
+                        void* grad_input, void* grad_weight, void* grad_offset, void* grad_mask,
+                        void* grad_bias, void* workspace, cudaStream_t st) {
   if (d.dtype == DCN_BFLOAT16) {
     using T = __nv_bfloat16;
     return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
-                            (const T*)mask, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
+                            (const T*)mask, saved, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
                             (T*)grad_mask, (T*)grad_bias, workspace, st);
   }
   using T = __half;
   return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
-                          (const T*)mask, (T*)grad_input, (T*)grad_weight, (T*)grad_offset, (T*)grad_mask,
-                          (T*)grad_bias, workspace, st);
+                          (const T*)mask, saved, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
+                          (T*)grad_mask, (T*)grad_bias, workspace, st);
 }
 
 }  // namespace dcn

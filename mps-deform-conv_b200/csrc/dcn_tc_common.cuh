@@ -173,8 +173,9 @@ struct KWalk {
 // One producer thread's share of a run of K chunks for one pixel tile: per
 // chunk it waits for its stage to be free, gathers 2 x 16 bytes of 4 corners,
 // blends, and writes its two 16-byte chunks of row r into the swizzled tile.
-// `stage_of(i)` returns (shared-memory tile base, empty-barrier, parity,
-// full-barrier) for the i-th chunk of the run; returns false if a wait expired.
+// `stage_of(i)` returns (shared-memory tile base, global tile copy or null,
+// empty-barrier, parity, full-barrier) for the i-th chunk of the run; returns
+// false if a wait expired.
 template <typename T, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
@@ -206,12 +207,18 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
       if (og1 != og0) raw1 = load_raw(g, off, msk, pc, og1, nx.t);
     }
     uint8_t* tile;
+    uint8_t* gtile;  // global copy of the tile image, or null
     uint32_t empty_bar, parity, full_bar;
-    stage_of(i, tile, empty_bar, parity, full_bar);
+    stage_of(i, tile, gtile, empty_bar, parity, full_bar);
+    const uint4 b0 = blend8<T>(v0, cs0.w), b1 = blend8<T>(v1, cs1.w);
+    const int o0 = r * 128 + ((cq ^ (r & 7)) << 4), o1 = r * 128 + (((cq + 4) ^ (r & 7)) << 4);
+    if (gtile) {  // streaming stores: keep L2 for the gather
+      __stcs(reinterpret_cast<uint4*>(gtile + o0), b0);
+      __stcs(reinterpret_cast<uint4*>(gtile + o1), b1);
+    }
     if (!mbar_wait(empty_bar, parity, abort_flag, status, code)) return false;
-    uint8_t* row = tile + r * 128;
-    *reinterpret_cast<uint4*>(row + ((cq ^ (r & 7)) << 4)) = blend8<T>(v0, cs0.w);
-    *reinterpret_cast<uint4*>(row + (((cq + 4) ^ (r & 7)) << 4)) = blend8<T>(v1, cs1.w);
+    *reinterpret_cast<uint4*>(tile + o0) = b0;
+    *reinterpret_cast<uint4*>(tile + o1) = b1;
     fence_async_shared();
     mbar_arrive(full_bar);
     kw = nx;

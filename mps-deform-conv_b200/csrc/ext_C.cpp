@@ -11,6 +11,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <optional>
 #include <tuple>
 #include <vector>
 
@@ -133,6 +134,46 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
   return out;
 }
 
+// Training forward: like deform_conv2d_forward, and also returns the device
+// state the backward can reuse (a uint8 tensor; empty when this problem keeps
+// nothing).
+std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_train(
+    const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
+    const at::Tensor& bias, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+    int64_t dilation_h, int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask) {
+  TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
+  check_cuda(weight, "weight", input);
+  check_cuda(offset, "offset", input);
+  const bool has_mask = use_mask && mask.numel() > 0;
+  if (has_mask) check_cuda(mask, "mask", input);
+  const bool has_bias = bias.defined() && bias.numel() > 0;
+  if (has_bias) check_cuda(bias, "bias", input);
+  TORCH_CHECK(weight.dim() == 4, "weight must be 4-D");
+  c10::cuda::CUDAGuard guard(input.device());
+  dcn_conv_desc d = make_desc(input, weight.size(0), weight.size(2), weight.size(3), stride_h,
+                              stride_w, pad_h, pad_w, dilation_h, dilation_w, n_weight_grps,
+                              n_offset_grps, has_mask);
+  TORCH_CHECK(weight.size(1) * n_weight_grps == input.size(1), "weight in_channels (",
+              weight.size(1), ") x n_weight_grps (", n_weight_grps, ") must equal in_channels (",
+              input.size(1), ")");
+  auto [oh, ow] = out_size(d);
+  check_offset_mask(d, offset, mask, oh, ow);
+  if (has_bias) TORCH_CHECK(bias.numel() == weight.size(0), "bias must have out_channels elements");
+  auto x = input.contiguous(), w = weight.contiguous(), off = offset.contiguous();
+  auto m = has_mask ? mask.contiguous() : at::Tensor();
+  auto b = has_bias ? bias.contiguous() : at::Tensor();
+  auto out = at::empty({d.batch, d.out_channels, oh, ow}, input.options());
+  const size_t sbytes = dcn_saved_state_bytes(&d);
+  auto saved = at::empty({(int64_t)sbytes}, input.options().dtype(at::kByte));
+  auto ws = workspace(dcn_forward_workspace_size(&d), input);
+  check_status(dcn_deform_conv2d_forward_train(&d, x.data_ptr(), w.data_ptr(), off.data_ptr(),
+                                               has_mask ? m.data_ptr() : nullptr,
+                                               has_bias ? b.data_ptr() : nullptr, out.data_ptr(),
+                                               sbytes ? saved.data_ptr() : nullptr, sbytes,
+                                               ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+  return {out, saved};
+}
+
 // Reference: deformable_im2col_mps, deform_conv2d_mps.mm:806-936.
 at::Tensor deformable_im2col(const at::Tensor& input, const at::Tensor& offset,
                              const at::Tensor& mask, int64_t kernel_h, int64_t kernel_w,
@@ -226,7 +267,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
     const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
     const at::Tensor& offset, const at::Tensor& mask, const at::Tensor& bias, int64_t stride_h,
     int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
-    int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask, std::vector<bool> output_mask) {
+    int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask, std::vector<bool> output_mask,
+    const std::optional<at::Tensor>& saved_opt) {
   TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
   check_cuda(grad_output, "grad_output", input);
   check_cuda(weight, "weight", input);
@@ -257,10 +299,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
   if (output_mask[4] && has_bias) gb = at::empty({d.out_channels}, input.options());
   auto ws = workspace(dcn_backward_workspace_size(&d), input);
   auto ptr = [](const at::Tensor& t) -> void* { return t.defined() ? t.data_ptr() : nullptr; };
-  check_status(dcn_deform_conv2d_backward(&d, go.data_ptr(), x.data_ptr(), w.data_ptr(),
-                                          off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
-                                          ptr(gin), ptr(gw), ptr(goff), ptr(gm), ptr(gb),
-                                          ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+  const at::Tensor saved = saved_opt.has_value() ? *saved_opt : at::Tensor();
+  const bool has_saved = saved.defined() && saved.numel() > 0;
+  if (has_saved) {
+    TORCH_CHECK(saved.is_cuda() && saved.device() == input.device() && saved.scalar_type() == at::kByte &&
+                    saved.is_contiguous(),
+                "saved state must be a contiguous uint8 tensor on the input's device");
+  }
+  check_status(dcn_deform_conv2d_backward_train(
+      &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
+      has_saved ? saved.data_ptr() : nullptr, has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw),
+      ptr(goff), ptr(gm), ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
   return {gin, gw, goff, gm, gb};
 }
 
@@ -296,7 +345,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("mask"), py::arg("bias"), py::arg("stride_h"), py::arg("stride_w"),
         py::arg("pad_h"), py::arg("pad_w"), py::arg("dilation_h"), py::arg("dilation_w"),
         py::arg("n_weight_grps"), py::arg("n_offset_grps"), py::arg("use_mask"),
-        py::arg("output_mask") = std::vector<bool>{true, true, true, true, true});
+        py::arg("output_mask") = std::vector<bool>{true, true, true, true, true},
+        py::arg("saved") = py::none());
+  m.def("deform_conv2d_forward_train", &deform_conv2d_forward_train,
+        "Forward that also returns the device state its backward reuses: (output, saved)");
   m.def("uses_tensor_cores", &uses_tensor_cores, "True when the tcgen05 kernels run this problem");
   m.def("device_status", &device_status, "Raise if a kernel's bounded wait expired");
   m.def("abi_version", &dcn_abi_version);

@@ -26,6 +26,23 @@ _lib_lock = threading.Lock()
 # B200 runs bf16 natively, so nothing is ever converted or warned about.
 _bf16_warned = False
 
+# Training cache: when the weight needs a gradient, the forward keeps its
+# gathered column tiles and the channels-last input copy on the device for
+# the backward (about B*Ho*Wo*C*kh*kw*2 bytes per layer between forward and
+# backward), so the backward neither re-lays-out the input nor gathers the
+# columns again.  The reference rebuilds its column buffer in the backward
+# instead (mps_deform_conv/__init__.py:266-273).
+_training_cache = True
+
+
+def set_training_cache(enabled: bool) -> None:
+    """Keep (True, default) or drop (False) the forward's column tiles for the backward.
+
+    Dropping them saves device memory between forward and backward at the
+    cost of a second bilinear gather in the weight-gradient pass."""
+    global _training_cache
+    _training_cache = bool(enabled)
+
 
 def _load_library():
     """Load the native extension; fail loudly when it is missing."""
@@ -183,14 +200,23 @@ class _DeformConv2dFunction(torch.autograd.Function):
         bias_t = bias if bias is not None else torch.empty(0, device=input.device, dtype=input.dtype)
         mask_t = mask if mask is not None else torch.empty(0, device=input.device, dtype=input.dtype)
 
-        output = lib.deform_conv2d_forward(
-            input, weight, offset, mask_t, bias_t,
-            stride_h, stride_w, pad_h, pad_w,
-            dilation_h, dilation_w,
-            n_weight_grps, n_offset_grps, use_mask,
-        )
+        if _training_cache and ctx.needs_input_grad[2]:
+            output, saved = lib.deform_conv2d_forward_train(
+                input, weight, offset, mask_t, bias_t,
+                stride_h, stride_w, pad_h, pad_w,
+                dilation_h, dilation_w,
+                n_weight_grps, n_offset_grps, use_mask,
+            )
+        else:
+            output = lib.deform_conv2d_forward(
+                input, weight, offset, mask_t, bias_t,
+                stride_h, stride_w, pad_h, pad_w,
+                dilation_h, dilation_w,
+                n_weight_grps, n_offset_grps, use_mask,
+            )
+            saved = None
 
-        ctx.save_for_backward(input, offset, weight, mask_t if use_mask else None)
+        ctx.save_for_backward(input, offset, weight, mask_t if use_mask else None, saved)
         ctx.bias_exists = bias is not None
         ctx.stride = stride
         ctx.padding = padding
@@ -202,7 +228,7 @@ class _DeformConv2dFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output: Tensor):
-        input, offset, weight, mask = ctx.saved_tensors
+        input, offset, weight, mask, saved = ctx.saved_tensors
         stride_h, stride_w = ctx.stride
         pad_h, pad_w = ctx.padding
         dilation_h, dilation_w = ctx.dilation
@@ -218,6 +244,7 @@ class _DeformConv2dFunction(torch.autograd.Function):
             grad_output, input, weight, offset, mask_t, bias_t,
             stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
             ctx.n_weight_grps, ctx.n_offset_grps, use_mask, output_mask,
+            saved,
         )
         return (grad_input, grad_offset, grad_weight, grad_bias,
                 None, None, None, grad_mask, None, None, None)
@@ -387,4 +414,5 @@ def is_available() -> bool:
     return torch.cuda.is_available()
 
 
-__all__ = ["deform_conv2d", "DeformConv2d", "ModulatedDeformConv2d", "is_available", "__version__"]
+__all__ = ["deform_conv2d", "DeformConv2d", "ModulatedDeformConv2d", "is_available", "__version__",
+           "set_training_cache"]

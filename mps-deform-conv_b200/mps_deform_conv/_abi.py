@@ -58,6 +58,10 @@ SIGNATURES = {
     "dcn_deform_conv2d_backward_offset_mask": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V]),
     "dcn_backward_workspace_size": (_SZ, [_D]),
     "dcn_deform_conv2d_backward": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "dcn_saved_state_bytes": (_SZ, [_D]),
+    "dcn_deform_conv2d_forward_train": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
+    "dcn_deform_conv2d_backward_train": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V,
+                                                        _V, _SZ, _V]),
     "dcn_device_status": (ctypes.c_int, [_V]),
     "dcn_uses_tensor_cores": (ctypes.c_int, [_D]),
 }

@@ -115,3 +115,72 @@ def test_tc_backward_output_subsets(mask_sel, cuda):
             assert rel_err(to_np(pz), to_np(f)) <= 1e-2
         else:
             assert pz is None
+
+
+@pytest.mark.parametrize("cache", [True, False])
+@pytest.mark.parametrize("name", ["c64_og8_far", "c128_g2_og4_dil2", "c192_co96_tail"])
+def test_tc_autograd_training_cache(name, cache, cuda):
+    """Autograd training step with the forward's saved state (column tiles +
+    channels-last input) kept for the backward, and without it."""
+    import mps_deform_conv as mdc
+    T = _make(SHAPES[name], torch.bfloat16, cuda, seed=11)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    leaves = {k: T[k].clone().requires_grad_(True) for k in ("input", "offset", "weight", "bias", "mask")
+              if T[k] is not None}
+    mdc.set_training_cache(cache)
+    try:
+        out = mdc.deform_conv2d(leaves["input"], leaves["offset"], leaves["weight"], leaves.get("bias"),
+                                st, pd, dl, leaves.get("mask"))
+        out.backward(T["grad_output"])
+    finally:
+        mdc.set_training_cache(True)
+    torch.cuda.synchronize()
+    ref_out = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                                st, pd, dl, T["mask"], T["bias"] is not None)
+    tol = TOL["bfloat16"]
+    assert rel_err(to_np(out), ref_out) <= tol
+    assert rel_err(to_np(leaves["input"].grad), rgi) <= tol
+    assert rel_err(to_np(leaves["offset"].grad), rgoff) <= tol
+    assert rel_err(to_np(leaves["weight"].grad), rgw) <= tol
+    if "bias" in leaves:
+        assert rel_err(to_np(leaves["bias"].grad), rgb) <= tol
+    if "mask" in leaves:
+        assert rel_err(to_np(leaves["mask"].grad), rgm) <= tol
+
+
+def test_abi_training_pair_matches_plain_calls(cuda):
+    """dcn_deform_conv2d_forward_train / _backward_train through ctypes give the
+    same results as the plain forward / backward."""
+    import ctypes
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    T = _make(SHAPES["c128_g2_og4_dil2"], torch.float16, cuda, seed=13)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    d = _abi.desc_for(T["input"], T["weight"], T["offset"], st, pd, dl, T["mask"])
+    nbytes = lib.dcn_saved_state_bytes(ctypes.byref(d))
+    assert nbytes > 0
+    saved = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+    oh, ow = _abi.output_size(d)
+    out = torch.empty((d.batch, d.out_channels, oh, ow), device=cuda, dtype=torch.float16)
+    wsz = lib.dcn_forward_workspace_size(ctypes.byref(d))
+    ws = torch.empty(max(wsz, 1), dtype=torch.uint8, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    p = lambda t: None if t is None else t.data_ptr()
+    _abi.check(lib.dcn_deform_conv2d_forward_train(ctypes.byref(d), p(T["input"]), p(T["weight"]),
+                                                   p(T["offset"]), p(T["mask"]), p(T["bias"]), p(out),
+                                                   p(saved), nbytes, p(ws), wsz, stream))
+    grads = [torch.empty_like(T[k]) for k in ("input", "weight", "offset", "mask")] + \
+        [torch.empty_like(T["bias"])]
+    bsz = lib.dcn_backward_workspace_size(ctypes.byref(d))
+    bws = torch.empty(max(bsz, 1), dtype=torch.uint8, device=cuda)
+    _abi.check(lib.dcn_deform_conv2d_backward_train(ctypes.byref(d), p(T["grad_output"]), p(T["input"]),
+                                                    p(T["weight"]), p(T["offset"]), p(T["mask"]), p(saved),
+                                                    nbytes, *[p(g) for g in grads], p(bws), bsz, stream))
+    ref_out = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    gi, goff, gw, gb, gm = _abi.call_backward(T["grad_output"], T["input"], T["offset"], T["weight"],
+                                              st, pd, dl, T["mask"], with_bias=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out)
+    for a_, b_ in zip(grads, (gi, gw, goff, gm, gb)):
+        assert rel_err(to_np(a_), to_np(b_)) <= 1e-2
