@@ -226,29 +226,48 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
 // ---------------------------------------------------------------- wgrad from saved columns
 // Same GEMM as dcn_wgrad_tc_kernel, but the column tiles are the forward's
 // (saved in their shared-memory image) and arrive by bulk copy: no gather.
-// Warps 0-3 epilogue, warp 4 MMA, warp 5 loader (gOt by TMA + column tiles).
+// The reduction over pixels runs in 64-pixel slices; one stage holds the
+// slice of grad_output (A, MN-major [64 px][Cog]) and the same slice of all
+// nk column tiles of the CTA side by side (B, MN-major [64 px][nk*64]), so
+// each MMA is M=128 x N=64*nk x K=16 and reads few operand bytes per FLOP.
+// Warps 0-3 epilogue, warp 4 MMA, warp 5 loader.
 constexpr int WC_EPI_WARPS = 4;
 constexpr int WC_MMA_WARP = 4;
 constexpr int WC_NTHREADS = 192;
+constexpr int WC_SLICE = 64;                        // pixels per stage
+constexpr int WC_HALF_TILE = WC_SLICE * 128;        // 8 KB: 64 rows of 128 bytes
+
+struct WgradColsSmem {
+  uint32_t stage, a_bytes, b_bytes, bar, total;
+  int stages;
+};
+__host__ __device__ inline WgradColsSmem wgrad_cols_smem(int ncb_pad, int nkg, int stages) {
+  WgradColsSmem L;
+  L.a_bytes = (uint32_t)ncb_pad * WC_HALF_TILE;     // [64 px][64 co] blocks, ncb_pad = 2*mh
+  L.b_bytes = (uint32_t)nkg * WC_HALF_TILE;         // [64 px][64 ch] per K chunk
+  L.stage = L.a_bytes + L.b_bytes;
+  L.stages = stages;
+  L.bar = stages * L.stage;
+  L.total = L.bar + (2 * stages + 2) * 8 + 16;
+  return L;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(WC_NTHREADS, 1)
 dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
-                         const __grid_constant__ CUtensorMap tmap_go) {
+                         const __grid_constant__ CUtensorMap tmap_go64) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Geom& g = a.g;
-  const int AS = a.a_stages, BS = a.b_stages;
-  const WgradSmem L = wgrad_smem(a.mh, AS, BS);
+  const int S = a.b_stages;
+  const WgradColsSmem L = wgrad_cols_smem(2 * a.mh, a.nkg, S);
   const uint32_t sbase = smem_addr(smem);
   const uint32_t bar0 = sbase + L.bar;
-  auto a_full = [&](int s) { return bar0 + 8u * s; };
-  auto a_empty = [&](int s) { return bar0 + 8u * (AS + s); };
-  auto b_full = [&](int s) { return bar0 + 8u * (2 * AS + s); };
-  auto b_empty = [&](int s) { return bar0 + 8u * (2 * AS + BS + s); };
-  const uint32_t d_full = bar0 + 8u * (2 * AS + 2 * BS);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t d_full = bar0 + 8u * (2 * S);
   const uint32_t drain = d_full + 8u;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (2 * AS + 2 * BS + 2) * 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (2 * S + 2) * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -257,10 +276,10 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
   const int nk = min(a.nkg, a.nkc - k0);
   const int t0 = blockIdx.z * a.tiles_per_cta;
   const int nt = max(0, min(a.tiles_per_cta, a.n_tiles - t0));
+  const int nslices = nt * (BM / WC_SLICE);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < AS; ++s) { mbar_init(a_full(s), 1); mbar_init(a_empty(s), 1); }
-    for (int s = 0; s < BS; ++s) { mbar_init(b_full(s), 1); mbar_init(b_empty(s), 1); }
+    for (int s = 0; s < S; ++s) { mbar_init(full(s), 1); mbar_init(empty(s), 1); }
     mbar_init(d_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -277,7 +296,7 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
 
   if (warp < WC_EPI_WARPS) {
     // -------------------------------------------- epilogue: TMEM -> fp32 atomics
-    const bool ready = nt > 0 && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
+    const bool ready = nslices > 0 && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
     if (__all_sync(0xffffffffu, ready)) {
       tc_fence_after();
       const int q = warp;
@@ -286,7 +305,7 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
         const int co = h * BM + q * 32 + lane;
         const int kc = k0 + kcl;
         const int t = kc % g.T, cc = kc / g.T;
-        const uint32_t col = (uint32_t)((h * a.nkg + kcl) * 64);
+        const uint32_t col = (uint32_t)(h * a.nkg * 64 + kcl * 64);
 #pragma unroll 1
         for (int c16 = 0; c16 < 4; ++c16) {
           uint32_t v[16];
@@ -302,34 +321,33 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
     }
   } else if (warp == WC_MMA_WARP) {
     // -------------------------------------------- MMA issuer
-    if (lane == 0 && nt > 0) {
+    if (lane == 0 && nslices > 0) {
+      // up to 4 K chunks (N = 256) per MMA; a 5th..8th chunk goes to a second MMA
+      const int nsub = (nk + 3) / 4;
+      const uint32_t idesc0 = idesc_f16_major(BM, 64 * min(nk, 4), a.idesc != 0, true, true);
+      const uint32_t idesc1 = idesc_f16_major(BM, 64 * max(nk - 4, 1), a.idesc != 0, true, true);
       bool ok = true;
       int committed = 0;
-      for (int li = 0; li < nt && ok; ++li) {
-        const int as = li % AS;
-        ok = mbar_wait(a_full(as), (li / AS) & 1, abort_flag, a.status, ST_W_MMA);
+      for (int i = 0; i < nslices && ok; ++i) {
+        const int s = i % S;
+        ok = mbar_wait(full(s), (i / S) & 1, abort_flag, a.status, ST_W_MMA);
         if (!ok) break;
-        const uint32_t abase = sbase + L.a + as * L.a_stage;
-        for (int kcl = 0; kcl < nk && ok; ++kcl) {
-          const int j = li * nk + kcl;
-          const int s = j % BS;
-          ok = mbar_wait(b_full(s), (j / BS) & 1, abort_flag, a.status, ST_W_MMA);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t bbase = sbase + L.b + s * A_STAGE_BYTES;
-          for (int h = 0; h < a.mh; ++h) {
-            const uint32_t dcol = (uint32_t)((h * a.nkg + kcl) * 64);
+        tc_fence_after();
+        const uint32_t abase = sbase + s * L.stage;
+        const uint32_t bbase = abase + L.a_bytes;
+        for (int h = 0; h < a.mh; ++h) {
+          for (int sub = 0; sub < nsub; ++sub) {
 #pragma unroll
-            for (int kk = 0; kk < BM / 16; ++kk) {
-              const uint64_t ad = desc_mnmajor_sw128(abase + h * 2 * A_STAGE_BYTES + kk * 2048, A_STAGE_BYTES);
-              const uint64_t bd = desc_mnmajor_sw128(bbase + kk * 2048, A_STAGE_BYTES);
-              mma_f16(tmem + dcol, ad, bd, a.idesc, (li > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < WC_SLICE / 16; ++kk) {
+              const uint64_t ad = desc_mnmajor_sw128(abase + h * 2 * WC_HALF_TILE + kk * 2048, WC_HALF_TILE);
+              const uint64_t bd = desc_mnmajor_sw128(bbase + sub * 4 * WC_HALF_TILE + kk * 2048, WC_HALF_TILE);
+              mma_f16(tmem + (uint32_t)(h * a.nkg * 64 + sub * 256), ad, bd, sub ? idesc1 : idesc0,
+                      (i > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          mma_commit(b_empty(s));
-          ++committed;
         }
-        if (ok) mma_commit(a_empty(as));
+        mma_commit(empty(s));
+        ++committed;
       }
       if (ok) {
         mma_commit(d_full);
@@ -339,36 +357,29 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
       }
     }
   } else {
-    // -------------------------------------------- loader: gOt tiles (TMA) + column tiles (bulk)
-    if (lane == 0 && nt > 0) {
-      const uint32_t abytes = (uint32_t)a.ncb * A_STAGE_BYTES;
-      int a_issued = 0, b_issued = 0;
-      bool ok = true;
-      for (int li = 0; li < nt && ok; ++li) {
-        const int as = li % AS;
-        ok = mbar_wait(a_empty(as), ((li / AS) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD);
-        if (!ok) break;
-        mbar_arrive_expect_tx(a_full(as), abytes);
-        const uint32_t dst = sbase + L.a + as * L.a_stage;
+    // -------------------------------------------- loader
+    if (lane == 0 && nslices > 0) {
+      const uint32_t bytes = (uint32_t)a.ncb * WC_HALF_TILE + (uint32_t)nk * WC_HALF_TILE;
+      int issued = 0;
+      for (int i = 0; i < nslices; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD)) break;
+        mbar_arrive_expect_tx(full(s), bytes);
+        const int tile = t0 + i / (BM / WC_SLICE), half = i % (BM / WC_SLICE);
+        const uint32_t dst = sbase + s * L.stage;
         for (int cb = 0; cb < a.ncb; ++cb)
-          tma_load_2d(dst + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, (t0 + li) * BM, a_full(as));
-        ++a_issued;
+          tma_load_2d(dst + cb * WC_HALF_TILE, &tmap_go64, grp * g.Cog + cb * 64, tile * BM + half * WC_SLICE,
+                      full(s));
         const uint8_t* src = static_cast<const uint8_t*>(cols) +
-                             (((size_t)grp * a.n_tiles + t0 + li) * a.nkc + k0) * (size_t)A_STAGE_BYTES;
-        for (int kcl = 0; kcl < nk; ++kcl) {
-          const int j = li * nk + kcl;
-          const int s = j % BS;
-          ok = mbar_wait(b_empty(s), ((j / BS) & 1) ^ 1, abort_flag, a.status, ST_W_LOAD);
-          if (!ok) break;
-          mbar_arrive_expect_tx(b_full(s), A_STAGE_BYTES);
-          bulk_g2s(sbase + L.b + s * A_STAGE_BYTES, src + (size_t)kcl * A_STAGE_BYTES, A_STAGE_BYTES, b_full(s));
-          ++b_issued;
-        }
+                             (((size_t)grp * a.n_tiles + tile) * a.nkc + k0) * (size_t)A_STAGE_BYTES +
+                             (size_t)half * WC_HALF_TILE;
+        for (int kcl = 0; kcl < nk; ++kcl)
+          bulk_g2s(dst + L.a_bytes + kcl * WC_HALF_TILE, src + (size_t)kcl * A_STAGE_BYTES, WC_HALF_TILE,
+                   full(s));
+        ++issued;
       }
-      for (int li = (a_issued > AS ? a_issued - AS : 0); li < a_issued; ++li)
-        mbar_wait(a_full(li % AS), (li / AS) & 1, abort_flag, a.status, ST_W_LOAD);
-      for (int j = (b_issued > BS ? b_issued - BS : 0); j < b_issued; ++j)
-        mbar_wait(b_full(j % BS), (j / BS) & 1, abort_flag, a.status, ST_W_LOAD);
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+        mbar_wait(full(i % S), (i / S) & 1, abort_flag, a.status, ST_W_LOAD);
     }
   }
 
@@ -910,11 +921,20 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.tmem_cols = pow2_cols(a.mh * a.nkg * 64);
     const int smem = (int)wgrad_smem(a.mh, a.a_stages, a.b_stages).total + 1024;
     if (cols) {
+      CUtensorMap tmap64;  // grad_output slices of 64 pixels
+      if (!make_tmap_2d(&tmap64, got, bf16, (uint64_t)g.P, (uint64_t)g.Co, WC_SLICE, 64))
+        return cudaErrorInvalidValue;
+      WgradArgs c = a;
+      c.idesc = bf16 ? 1u : 0u;  // operand type flag; the kernel builds N = 64*nk per CTA
+      c.b_stages = 4;
+      while (c.b_stages > 2 && wgrad_cols_smem(2 * c.mh, c.nkg, c.b_stages).total + 1024 > 225 * 1024) --c.b_stages;
+      const int csmem = (int)wgrad_cols_smem(2 * c.mh, c.nkg, c.b_stages).total + 1024;
+      if (csmem > 225 * 1024) return cudaErrorInvalidConfiguration;
       if ((e = cudaFuncSetAttribute(dcn_wgrad_cols_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    smem)) != cudaSuccess)
+                                    csmem)) != cudaSuccess)
         return e;
       KernelScope ks("dcn_wgrad_cols_tc", st);
-      dcn_wgrad_cols_tc_kernel<T><<<dim3(kgroups, g.G, splits), WC_NTHREADS, smem, st>>>(a, cols, tmap);
+      dcn_wgrad_cols_tc_kernel<T><<<dim3(kgroups, g.G, splits), WC_NTHREADS, csmem, st>>>(c, cols, tmap64);
     } else {
       if ((e = cudaFuncSetAttribute(dcn_wgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
         return e;
