@@ -301,6 +301,10 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(p)
 
+    suite = None
+    if world == 1 and not args.no_suite:
+        suite = run_suite(dev, skip=p.name)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s",
@@ -321,6 +325,7 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
+            "other_workloads": suite,
             "tensor_cores": bool(mdc._get_lib().uses_tensor_cores(
                 x, w, p.stride, p.stride, p.padding, p.padding, p.dilation, p.dilation,
                 p.groups, p.offset_groups, p.use_mask)),
@@ -330,6 +335,59 @@ def run_ours(args):
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_suite(dev, skip, steps=5, warmup=3):
+    """Short device-timed fwd(+bwd) runs of the other workloads (N=1): one
+    entry per problem with ms/step, TFLOP/s, samples/s, which kernel family
+    ran it and its top kernels.  Inputs stay resident; the L2 is flushed
+    between steps."""
+    import mps_deform_conv as mdc
+    from mps_deform_conv import _abi
+    res = {}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for name, p in PROBLEMS.items():
+        if name == skip:
+            continue
+        inp = make_inputs(p, dev)
+        st, pd, dl = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
+        leaves = [t.requires_grad_(p.training) if t is not None else None
+                  for t in (inp["input"], inp["offset"], inp["weight"], inp["bias"], inp["mask"])]
+        lv = [t for t in leaves if t is not None]
+
+        def step():
+            out = mdc.deform_conv2d(leaves[0], leaves[1], leaves[2], leaves[3], st, pd, dl, leaves[4])
+            if p.training:
+                torch.autograd.grad(out, lv, inp["grad_output"])
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        _abi.profile_enable(True)
+        ms = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            torch.cuda.synchronize()
+            ms += a.elapsed_time(b)
+        _abi.profile_enable(False)
+        prof = sorted(_abi.profile_summary(), key=lambda r: -r[2])
+        ms /= steps
+        tc = bool(mdc._get_lib().uses_tensor_cores(inp["input"], inp["weight"], p.stride, p.stride, p.padding,
+                                                   p.padding, p.dilation, p.dilation, p.groups,
+                                                   p.offset_groups, p.use_mask))
+        res[name] = {"description": p.description, "pass": "fwd+bwd" if p.training else "fwd",
+                     "ms_per_step": round(ms, 4), "tflops": round(p.flops() / (ms / 1e3) / 1e12, 3),
+                     "samples_per_s": round(p.batch / (ms / 1e3), 1),
+                     "min_hbm_bytes": p.min_hbm_bytes(),
+                     "hbm_frac_of_measured": round(p.min_hbm_bytes() / (ms / 1e3) / 1e9 / load_peaks()["hbm_gbs"], 4),
+                     "kernels": "tcgen05" if tc else "simt",
+                     "top": [{"name": n, "ms_per_step": round(t / steps, 4)} for n, l, t in prof[:3]]}
+        del inp, leaves, lv
+        torch.cuda.empty_cache()
+    return res
 
 
 def kernel_roofline(p, nb, name):
@@ -431,6 +489,7 @@ def main():
     ap.add_argument("--workload", default="c5_train_bf16", choices=sorted(PROBLEMS))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-suite", action="store_true", help="skip the short runs of the other workloads")
     ap.add_argument("--traffic-per-launch", type=float, default=None,
                     help="ncu dram bytes per launch of the dominant kernel, if captured")
     args = ap.parse_args()

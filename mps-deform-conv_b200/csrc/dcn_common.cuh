@@ -4,9 +4,9 @@
 //
 // Sampling semantics follow the reference kernels in
 // mps_deform_conv/csrc/deform_conv2d_mps.mm: bilinear_interpolate (:41-68) and
-// get_coordinate_weight (:72-102).  Coordinates are always computed in fp32
-// (the reference's fp16 kernel computes them in half at :238-239, which
-// torchvision does not; fp32 is what keeps parity with torchvision).
+// get_coordinate_weight (:72-102).  Sampling points are split into an exact
+// integer floor and an fp32 fraction (sample_pos); the reference's fp16 kernel
+// computes them in half (:238-239), which torchvision does not.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -66,20 +66,40 @@ inline Geom make_geom(const dcn_conv_desc& d) {
   return g;
 }
 
+// Sampling point of a tap: the integer base position (oy*stride - pad +
+// i*dilation) plus an offset.  The floor and the fraction are taken from the
+// offset alone -- y0 = base + floor(dy), fy = dy - floor(dy) -- so the choice
+// of corners is exact (it equals the float64 decision) even when base + dy
+// lies within an fp32 rounding step of an integer, where the bilinear
+// derivative jumps.
+struct SamplePos {
+  int y0, x0;     // floor of the sampling point
+  float fy, fx;   // fractional parts, in [0, 1]
+};
+
+__device__ __forceinline__ SamplePos sample_pos(int base_y, int base_x, float dy, float dx) {
+  const float ffy = floorf(dy), ffx = floorf(dx);
+  SamplePos s;
+  s.y0 = base_y + (int)ffy;
+  s.x0 = base_x + (int)ffx;
+  s.fy = dy - ffy;
+  s.fx = dx - ffx;
+  return s;
+}
+
 // Sampling point of tap t at output pixel p = oy*Wo+ox of image b, offset
 // group o (reference :154-168).  Returns the mask value through *m.
 template <typename T>
-__device__ __forceinline__ void sample_point(const Geom& g, const T* __restrict__ offset,
-                                             const T* __restrict__ mask, int b, int o, int t,
-                                             int p, float* y, float* x, float* m) {
+__device__ __forceinline__ SamplePos sample_point(const Geom& g, const T* __restrict__ offset,
+                                                  const T* __restrict__ mask, int b, int o, int t,
+                                                  int p, float* m) {
   const int oy = p / g.Wo, ox = p - oy * g.Wo;
   const int i = t / g.kw, j = t - i * g.kw;
   const long long obase = ((long long)(b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + p;
   const float dy = to_f(offset[obase]);
   const float dx = to_f(offset[obase + g.HWo]);
-  *y = (float)(oy * g.sh - g.ph) + (float)(i * g.dh) + dy;
-  *x = (float)(ox * g.sw - g.pw) + (float)(j * g.dw) + dx;
   *m = g.use_mask ? to_f(mask[((long long)(b * g.OG + o) * g.T + t) * g.HWo + p]) : 1.0f;
+  return sample_pos(oy * g.sh - g.ph + i * g.dh, ox * g.sw - g.pw + j * g.dw, dy, dx);
 }
 
 // Corner set of one bilinear sample.  w[k] is the weight of corner k
@@ -92,12 +112,14 @@ struct Corners {
   int idx[4];
 };
 
-__device__ __forceinline__ Corners corners_of(float y, float x, int H, int W) {
+__device__ __forceinline__ Corners corners_of(const SamplePos& s, int H, int W) {
   Corners c;
-  const bool inside = (y > -1.0f) && (y < (float)H) && (x > -1.0f) && (x < (float)W);
-  const float fy = floorf(y), fx = floorf(x);
-  const int y0 = (int)fy, x0 = (int)fx, y1 = y0 + 1, x1 = x0 + 1;
-  const float ly = y - fy, lx = x - fx, hy = 1.0f - ly, hx = 1.0f - lx;
+  // y > -1 and y < H with y = y0 + fy, fy in [0, 1]
+  const bool in_y = (s.y0 > -1 || (s.y0 == -1 && s.fy > 0.0f)) && s.y0 < H;
+  const bool in_x = (s.x0 > -1 || (s.x0 == -1 && s.fx > 0.0f)) && s.x0 < W;
+  const bool inside = in_y && in_x;
+  const int y0 = s.y0, x0 = s.x0, y1 = y0 + 1, x1 = x0 + 1;
+  const float ly = s.fy, lx = s.fx, hy = 1.0f - ly, hx = 1.0f - lx;
   const bool vy0 = inside && y0 >= 0, vy1 = inside && y1 <= H - 1;
   const bool vx0 = x0 >= 0, vx1 = x1 <= W - 1;
   c.w[0] = (vy0 && vx0) ? hy * hx : 0.0f;
@@ -126,12 +148,11 @@ struct CoordCorners {
   int idx[4];
 };
 
-__device__ __forceinline__ CoordCorners coord_corners_of(float y, float x, int H, int W) {
+__device__ __forceinline__ CoordCorners coord_corners_of(const SamplePos& s, int H, int W) {
   CoordCorners c;
-  const float fly = floorf(y), flx = floorf(x);
-  const int y0 = (int)fly, x0 = (int)flx, y1 = y0 + 1, x1 = x0 + 1;
-  c.fy = y - fly;
-  c.fx = x - flx;
+  const int y0 = s.y0, x0 = s.x0, y1 = y0 + 1, x1 = x0 + 1;
+  c.fy = s.fy;
+  c.fx = s.fx;
   const bool vy0 = 0 <= y0 && y0 < H, vy1 = 0 <= y1 && y1 < H;
   const bool vx0 = 0 <= x0 && x0 < W, vx1 = 0 <= x1 && x1 < W;
   c.v[0] = vy0 && vx0; c.v[1] = vy0 && vx1; c.v[2] = vy1 && vx0; c.v[3] = vy1 && vx1;

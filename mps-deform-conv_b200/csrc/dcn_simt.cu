@@ -22,9 +22,9 @@ __device__ __forceinline__ float column_value(const Geom& g, const T* __restrict
                                               const T* __restrict__ offset,
                                               const T* __restrict__ mask, int b, int c, int t,
                                               int p) {
-  float y, x, m;
-  sample_point(g, offset, mask, b, c / g.cpo, t, p, &y, &x, &m);
-  const Corners cs = corners_of(y, x, g.H, g.W);
+  float m;
+  const SamplePos sp = sample_point(g, offset, mask, b, c / g.cpo, t, p, &m);
+  const Corners cs = corners_of(sp, g.H, g.W);
   const T* plane = input + ((long long)b * g.C + c) * g.H * g.W;
   return m * bilinear(plane, cs);
 }
@@ -200,9 +200,9 @@ __global__ void col2im_kernel(Geom g, const TC* __restrict__ gcol, const T* __re
     const long long row = e / g.P, n = e - row * g.P;
     const int c = (int)(row / g.T), t = (int)(row - (long long)c * g.T);
     const int b = (int)(n / g.HWo), p = (int)(n - (long long)b * g.HWo);
-    float y, x, m;
-    sample_point(g, off, msk, b, c / g.cpo, t, p, &y, &x, &m);
-    const Corners cs = corners_of(y, x, g.H, g.W);
+    float m;
+    const SamplePos sp = sample_point(g, off, msk, b, c / g.cpo, t, p, &m);
+    const Corners cs = corners_of(sp, g.H, g.W);
     const float v = m * to_f(gcol[e]);
     float* plane = gin + ((long long)b * g.C + c) * g.H * g.W;
 #pragma unroll
@@ -224,10 +224,10 @@ __global__ void col2im_coord_kernel(Geom g, const TC* __restrict__ gcol, const T
     const int t = (int)(r % g.T); r /= g.T;
     const int o = (int)(r % g.OG);
     const int b = (int)(r / g.OG);
-    float y, xx, m;
-    sample_point(g, off, msk, b, o, t, p, &y, &xx, &m);
-    const CoordCorners cc = coord_corners_of(y, xx, g.H, g.W);
-    const Corners cs = corners_of(y, xx, g.H, g.W);
+    float m;
+    const SamplePos sp = sample_point(g, off, msk, b, o, t, p, &m);
+    const CoordCorners cc = coord_corners_of(sp, g.H, g.W);
+    const Corners cs = corners_of(sp, g.H, g.W);
     float gy = 0.f, gx = 0.f, gm = 0.f;
     for (int cl = 0; cl < g.cpo; ++cl) {
       const int c = o * g.cpo + cl;

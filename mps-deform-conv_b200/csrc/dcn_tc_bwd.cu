@@ -551,10 +551,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           if (o != coord_o) {
             coord_o = o;
             const RawSample<T> raw = load_raw(g, off, msk, pc, o, kw.t);
-            const float y = (float)(pc.y0 + kw.ti * g.dh) + to_f(raw.dy);
-            const float x = (float)(pc.x0 + kw.tj * g.dw) + to_f(raw.dx);
-            const Corners cs = corners_of(y, x, g.H, g.W);
-            const CoordCorners c4 = coord_corners_of(y, x, g.H, g.W);
+            const SamplePos sp =
+                sample_pos(pc.y0 + kw.ti * g.dh, pc.x0 + kw.tj * g.dw, to_f(raw.dy), to_f(raw.dx));
+            const Corners cs = corners_of(sp, g.H, g.W);
+            const CoordCorners c4 = coord_corners_of(sp, g.H, g.W);
             cm = pc.valid ? to_f(raw.m) : 0.f;
             cfy = c4.fy;
             cfx = c4.fx;

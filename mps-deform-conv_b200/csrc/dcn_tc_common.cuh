@@ -101,9 +101,8 @@ template <typename T>
 __device__ __forceinline__ CornerSet corner_set(const Geom& g, const PixelCtx& pc, const RawSample<T>& r,
                                                 int ti, int tj) {
   CornerSet cs;
-  const float y = (float)(pc.y0 + ti * g.dh) + to_f(r.dy);
-  const float x = (float)(pc.x0 + tj * g.dw) + to_f(r.dx);
-  const Corners c = corners_of(y, x, g.H, g.W);
+  const SamplePos sp = sample_pos(pc.y0 + ti * g.dh, pc.x0 + tj * g.dw, to_f(r.dy), to_f(r.dx));
+  const Corners c = corners_of(sp, g.H, g.W);
   const float m = pc.valid ? to_f(r.m) : 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {

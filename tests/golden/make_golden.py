@@ -33,6 +33,7 @@ CASES = {
     "ref_grad_case":     (1, 4, 6, 6, 4, 1, 1, (3, 3), (1, 1), (0, 0), (1, 1), False, False, "small"),
     "ref_bench_like":    (1, 8, 9, 9, 8, 1, 1, (3, 3), (1, 1), (0, 0), (1, 1), False, False, "small"),
     "empty_batch":       (0, 4, 5, 5, 4, 1, 1, (3, 3), (1, 1), (1, 1), (1, 1), True, True, "n1"),
+    "near_integer_offsets": (2, 4, 7, 8, 3, 1, 2, (3, 3), (1, 1), (1, 1), (1, 1), True, True, "near_int"),
 }
 
 
@@ -58,6 +59,14 @@ def make_case(name, spec, seed):
         # points and on the -1 / H borders, which exercises every validity branch
         off = torch.randint(-3, 4, oshape, generator=g).to(dt)
         off += (torch.randint(0, 2, oshape, generator=g).to(dt)) * 0.5
+    elif okind == "near_int":
+        # within +-2e-6 of an integer (+-n * 2^-22, exactly representable in
+        # fp32): base + offset sits within an fp32 rounding step of a grid
+        # line, where the bilinear derivative jumps
+        off = torch.randint(-3, 4, oshape, generator=g).to(dt)
+        n = torch.randint(1, 9, oshape, generator=g).to(dt)
+        sgn = torch.randint(0, 2, oshape, generator=g).to(dt) * 2 - 1
+        off += sgn * n * 2.0 ** -22
     else:
         raise ValueError(okind)
     mask = torch.sigmoid(torch.randn(B, og * kh * kw, Ho, Wo, generator=g, dtype=dt)) if use_mask else None

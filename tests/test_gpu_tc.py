@@ -21,6 +21,7 @@ SHAPES = {
     "c128_co256_s2": (1, 128, 14, 13, 256, 1, 1, 3, 2, 1, 1, True, False, 1.5),
     "c64_co512_nomask": (1, 64, 8, 9, 512, 1, 1, 3, 1, 1, 1, False, True, 1.0),
     "c192_co96_tail": (3, 192, 7, 9, 96, 1, 2, 3, 1, 1, 1, True, True, 2.0),
+    "c64_og8_near_int": (2, 64, 10, 12, 64, 1, 8, 3, 1, 1, 1, True, True, "near_int"),
 }
 
 
@@ -31,7 +32,11 @@ def _make(spec, dtype, dev, seed=0):
     Wo = (W + 2 * p - (d * (k - 1) + 1)) // s + 1
     x = torch.randn(B, C, H, W, generator=g)
     w = torch.randn(Co, C // G, k, k, generator=g) / np.sqrt(C // G * k * k)
-    off = torch.randn(B, 2 * og * k * k, Ho, Wo, generator=g) * osc
+    if osc == "near_int":  # within +-2e-6 of integers: exact-floor corner choice
+        off = torch.randint(-3, 4, (B, 2 * og * k * k, Ho, Wo), generator=g).float()
+        off += (torch.rand(B, 2 * og * k * k, Ho, Wo, generator=g) * 2 - 1) * 2e-6
+    else:
+        off = torch.randn(B, 2 * og * k * k, Ho, Wo, generator=g) * osc
     m = torch.sigmoid(torch.randn(B, og * k * k, Ho, Wo, generator=g)) if use_mask else None
     b = torch.randn(Co, generator=g) * 0.1 if use_bias else None
     go = torch.randn(B, Co, Ho, Wo, generator=g)
