@@ -51,59 +51,78 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled during the timed region.
+
+    Polls NVML (the counters behind nvidia-smi's clocks.sm / clocks.max.sm /
+    clocks_event_reasons.*) every ~2 ms from a thread, so even a timed region
+    of tens of milliseconds gets samples; falls back to `nvidia-smi -lms 20`."""
+    NAMES = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+             "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
+        self.samples = []   # (sm_mhz, max_mhz, reasons bitmask)
+        self.stop = threading.Event()
         self.proc = None
-        self.lines = []
+        self.t = None
+
+    def _poll_nvml(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self.stop.is_set():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                try:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((float(sm), float(mx), int(rs)))
+                time.sleep(0.002)
+        finally:
+            pynvml.nvmlShutdown()
+
+    def _poll_smi(self):
+        q = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+        self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={q}",
+                                      "--format=csv,noheader,nounits", "-lms", "20"],
+                                     stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            try:
+                self.samples.append((float(parts[0]), float(parts[1]), int(parts[2], 16)))
+            except Exception:
+                pass
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            import pynvml  # noqa: F401
+            target = self._poll_nvml
         except Exception:
-            self.proc = None
+            target = self._poll_smi
+        self.t = threading.Thread(target=target, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self.t is not None:
+            self.t.join(timeout=5)
 
     def summary(self):
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set()
+        for _, _, rs in self.samples:
+            for nm, bit in self.NAMES.items():
+                if rs & bit:
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(x[0] for x in self.samples),
+                "sm_max_mhz": max(x[1] for x in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "nvml"}
 
 
 def dist_setup():
@@ -287,7 +306,9 @@ def run_ours(args):
             unit = "GB/s"
         roof = {"kernel": name, "bound": rf["bound"], "achieved": round(achieved, 2),
                 "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
-                "traffic": args.traffic_per_launch, "avg_launch_ms": round(kms / nl, 4),
+                "traffic": args.traffic_per_launch or measured_traffic(p.name, name, nb),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch (profiles/dram_traffic.txt)",
+                "avg_launch_ms": round(kms / nl, 4),
                 "launches": nl, "peak_source": peaks["source"] + (" (sustained bf16)" if unit == "TFLOP/s" else ""),
                 "algorithmic_per_launch": rf["per_launch"], "note": rf["note"]}
 
@@ -390,6 +411,22 @@ def run_suite(dev, skip, steps=5, warmup=3):
     return res
 
 
+def measured_traffic(workload: str, kernel: str, batch: int):
+    """DRAM bytes per launch of `kernel` from the committed ncu summaries
+    (profiles/dram_traffic.txt: workload, kernel, batch, bytes per launch);
+    scaled by batch when measured on a different batch; None if absent."""
+    path = os.path.join(REPO, "profiles", "dram_traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 4 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel:
+                    return float(parts[3]) * batch / float(parts[2])
+    except OSError:
+        pass
+    return None
+
+
 def kernel_roofline(p, nb, name):
     """Algorithmic work per launch of a named kernel, for nb samples per launch."""
     ho, wo = p.out_hw
@@ -483,7 +520,7 @@ def cpu_baseline(p):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c5_train_bf16", choices=sorted(PROBLEMS))
