@@ -445,62 +445,83 @@ def kernel_roofline(p, nb, name):
 
 
 def run_e2e(p, inp, args, dev, world):
-    """Same step through the public API, inputs copied from pinned host memory
-    every step and the parameter gradients read back to the host."""
+    """Same step through the public API with host buffers: every step copies
+    its inputs (input, offset, mask, grad_output) from pinned host memory and
+    reads its result back (grad_weight and grad_bias when training, the output
+    otherwise).  The copies of step i+1 run on a copy stream while step i
+    computes (two device buffer sets), as a training input pipeline would."""
     import mps_deform_conv as mdc
     host = {k: (v.detach().cpu().pin_memory() if v is not None else None) for k, v in inp.items()}
+    keys = [k for k in ("input", "offset", "mask", "grad_output") if host[k] is not None]
+    if not p.training:
+        keys.remove("grad_output")
     stride, pad, dil = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
     dev_w = inp["weight"].detach().clone().requires_grad_(p.training)
     dev_b = inp["bias"].detach().clone().requires_grad_(p.training) if inp["bias"] is not None else None
-    h2d = sum(host[k].numel() * host[k].element_size() for k in ("input", "offset", "mask", "grad_output")
-              if host[k] is not None)
-    out_host = torch.empty(dev_w.shape, dtype=dev_w.dtype).pin_memory()
-    outb_host = torch.empty(dev_b.shape, dtype=dev_b.dtype).pin_memory() if dev_b is not None else None
-    d2h = out_host.numel() * out_host.element_size() + (outb_host.numel() * outb_host.element_size() if outb_host is not None else 0)
+    h2d = sum(host[k].numel() * host[k].element_size() for k in keys)
+    bufs = [{k: torch.empty_like(inp[k]) for k in keys} for _ in range(2)]
+    if p.training:
+        res_host = [torch.empty(dev_w.shape, dtype=dev_w.dtype).pin_memory()] + \
+            ([torch.empty(dev_b.shape, dtype=dev_b.dtype).pin_memory()] if dev_b is not None else [])
+    else:
+        res_host = [torch.empty((inp["input"].shape[0], p.out_channels) + p.out_hw, dtype=p.dtype).pin_memory()]
+    d2h = sum(t.numel() * t.element_size() for t in res_host)
+    main = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
 
-    def one():
-        x = host["input"].to(dev, non_blocking=True).requires_grad_(p.training)
-        off = host["offset"].to(dev, non_blocking=True).requires_grad_(p.training)
-        m = host["mask"].to(dev, non_blocking=True).requires_grad_(p.training) if host["mask"] is not None else None
-        go = host["grad_output"].to(dev, non_blocking=True)
+    def issue_copy(i):
+        b = bufs[i % 2]
+        with torch.cuda.stream(cs):
+            if i >= 2:
+                cs.wait_event(freed[i % 2])
+            for k in keys:
+                b[k].copy_(host[k], non_blocking=True)
+            copied[i % 2].record(cs)
+
+    def compute(i):
+        b = bufs[i % 2]
+        main.wait_event(copied[i % 2])
+        x = b["input"].detach().requires_grad_(p.training)
+        off = b["offset"].detach().requires_grad_(p.training)
+        m = b["mask"].detach().requires_grad_(p.training) if "mask" in b else None
         out = mdc.deform_conv2d(x, off, dev_w, dev_b, stride, pad, dil, m)
         if p.training:
             lv = [t for t in (x, off, dev_w, dev_b, m) if t is not None]
-            grads = torch.autograd.grad(out, lv, go)
-            gw = grads[2]
-            gb = grads[3] if dev_b is not None else None
+            grads = torch.autograd.grad(out, lv, b["grad_output"])
+            res = [grads[2]] + ([grads[3]] if dev_b is not None else [])
             if world > 1:
-                allreduce_param_grads([gw, gb])
-            out_host.copy_(gw, non_blocking=True)
-            if gb is not None:
-                outb_host.copy_(gb, non_blocking=True)
+                allreduce_param_grads(res)
         else:
-            out_host.copy_(dev_w, non_blocking=True)  # placeholder read of the same size
-    if not p.training:
-        o_host = torch.empty((inp["input"].shape[0], p.out_channels) + p.out_hw, dtype=p.dtype).pin_memory()
-        d2h = o_host.numel() * o_host.element_size()
+            res = [out]
+        for h, r in zip(res_host, res):
+            h.copy_(r, non_blocking=True)
+        freed[i % 2].record(main)
 
-        def one():  # noqa: F811
-            x = host["input"].to(dev, non_blocking=True)
-            off = host["offset"].to(dev, non_blocking=True)
-            m = host["mask"].to(dev, non_blocking=True) if host["mask"] is not None else None
-            out = mdc.deform_conv2d(x, off, dev_w, dev_b, stride, pad, dil, m)
-            o_host.copy_(out, non_blocking=True)
-    for _ in range(max(args.warmup, 3)):
-        one()
+    def run(n, start=None):
+        if start is not None:
+            cs.wait_event(start)
+        issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            compute(i)
+
+    run(max(args.warmup, 3))
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        one()
-    e.record()
+    s.record(main)
+    run(args.steps, start=s)
+    e.record(main)
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e), world)
     tflops = p.flops(p.batch) * args.steps / (ms / 1e3) / 1e12
     return {"value": round(tflops, 3), "unit": "TFLOP/s",
             "samples_per_s": round(p.batch * args.steps / (ms / 1e3), 2),
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "pipeline": "inputs of step i+1 copied on a second stream during step i"}
 
 
 def cpu_baseline(p):

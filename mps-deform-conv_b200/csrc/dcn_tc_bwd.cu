@@ -21,6 +21,8 @@
 //               range of pixel tiles, accumulates in TMEM and adds its partial
 //               gW into an fp32 buffer.
 //   finalize    fp32 accumulators -> caller dtype / NCHW.
+#include <cmath>
+
 #include "dcn_tc_common.cuh"
 
 namespace dcn {
@@ -467,6 +469,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, grp = blockIdx.y;
+  // this CTA's share of the K chunks (several CTAs per tile balance the waves
+  // when there are few tiles)
+  const int kc_lo = (int)(((long long)a.nkc * blockIdx.z) / gridDim.z);
+  const int nkc_cta = (int)(((long long)a.nkc * (blockIdx.z + 1)) / gridDim.z) - kc_lo;
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
@@ -504,13 +510,13 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
     const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
     const int qq = lane & 3, seg = qq >> 1;
     bool ok = true;
-    for (int i = e; i < a.nkc; i += D_NBUF) {
+    for (int i = e; i < nkc_cta; i += D_NBUF) {
       const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
       ok = __all_sync(0xffffffffu, ready);
       if (!ok) break;
       tc_fence_after();
       KWalk kw;
-      kw.start(g, i);
+      kw.start(g, kc_lo + i);
       const int cbase = grp * g.Cig + kw.cc * BK;
       int coord_o = -1, acc_o = -1;
       float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
@@ -646,7 +652,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
     if (lane == 0) {
       bool ok = mbar_wait(a_full, 0, abort_flag, a.status, ST_D_MMA);
       int committed = 0;
-      for (int i = 0; i < a.nkc && ok; ++i) {
+      for (int i = 0; i < nkc_cta && ok; ++i) {
         const int e = i % D_NBUF;
         ok = mbar_wait(d_empty(e), ((i / D_NBUF) & 1) ^ 1, abort_flag, a.status, ST_D_MMA);
         for (int kb = 0; kb < a.kb && ok; ++kb) {
@@ -678,9 +684,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       for (int cb = 0; cb < a.kb; ++cb)
         tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, tile * BM, a_full);
       // K blocks of W^T in order (kc, kb): block j = kc*KB + kb
-      const uint8_t* wbase = static_cast<const uint8_t*>(a.wdt) + (size_t)grp * a.nkc * a.kb * L.b_stage;
+      const uint8_t* wbase = static_cast<const uint8_t*>(a.wdt) +
+                             ((size_t)grp * a.nkc + kc_lo) * a.kb * L.b_stage;
       int issued = 0;
-      for (int j = 0; j < a.nkc * a.kb; ++j) {
+      for (int j = 0; j < nkc_cta * a.kb; ++j) {
         const int s = j % S;
         if (!mbar_wait(b_empty(s), ((j / S) & 1) ^ 1, abort_flag, a.status, ST_D_LOAD)) break;
         mbar_arrive_expect_tx(b_full(s), L.b_stage);
@@ -794,6 +801,25 @@ __global__ void nchw_to_nhwc_bwd_kernel(const T* __restrict__ x, T* __restrict__
   }
 }
 
+// Up to 4 fp32 -> T conversions in one grid-stride launch.
+struct ConvertJobs {
+  const float* src[4];
+  void* dst[4];
+  long long count[4];
+  int n;
+};
+
+template <typename T>
+__global__ void convert_multi_kernel(const ConvertJobs jobs) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (int j = 0; j < jobs.n; ++j) {
+    const float* __restrict__ s = jobs.src[j];
+    T* __restrict__ d = static_cast<T*>(jobs.dst[j]);
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < jobs.count[j]; e += stride)
+      d[e] = from_f<T>(s[e]);
+  }
+}
+
 // ================================================================ host
 struct BwdWs {
   size_t xh, got, wdt, acc, gi32, goff32, gmsk32, gw32, gb32, acc_bytes, total;
@@ -889,8 +915,17 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     const int smem = (int)dgrad_smem(KB, a.b_stages).total + 1024;
     if ((e = cudaFuncSetAttribute(dcn_dgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
       return e;
+    // split the K chunks of a tile over ksplit CTAs when that fills the last
+    // wave of 148 SMs (one CTA per SM) better; keep >= 4 chunks per CTA
+    int ksplit = 1;
+    double best = 0.0;
+    for (int k = 1; k <= 6 && nkc / k >= 4; ++k) {
+      const double waves = (double)n_tiles * g.G * k / 148.0;
+      const double eff = waves / std::ceil(waves);
+      if (eff > best + 0.05) { best = eff; ksplit = k; }
+    }
     KernelScope ks("dcn_dgrad_tc", st);
-    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G), D_NTHREADS, smem, st>>>(a, tmap);
+    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (gw) {
@@ -903,9 +938,11 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.nkg = (nkc + ngroups - 1) / ngroups;
     a.ncb = (g.Cog + 63) / 64;
     const int kgroups = (nkc + a.nkg - 1) / a.nkg;
+    // about one wave of CTAs: every CTA ends with an atomic add of its whole
+    // [Cog x nkg*64] partial, so more CTAs cost more atomics
     const int base = kgroups * g.G;
-    int splits = (2 * 148 + base - 1) / base;
-    if (splits > n_tiles) splits = n_tiles;
+    int splits = 148 / base;
+    if (splits > n_tiles / 4) splits = n_tiles / 4;
     if (splits < 1) splits = 1;
     a.tiles_per_cta = (n_tiles + splits - 1) / splits;
     splits = (n_tiles + a.tiles_per_cta - 1) / a.tiles_per_cta;
@@ -950,12 +987,21 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if (goff && (e = convert_f32<T>(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo, st)) != cudaSuccess) return e;
-  if (gmsk && g.use_mask &&
-      (e = convert_f32<T>(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo, st)) != cudaSuccess)
-    return e;
-  if (gw && (e = convert_f32<T>(gw32, gw, (long long)g.Co * g.Cig * g.T, st)) != cudaSuccess) return e;
-  if (gb && (e = convert_f32<T>(gb32, gb, (long long)g.Co, st)) != cudaSuccess) return e;
+  {  // offset / mask / weight / bias gradients: fp32 -> T in one launch
+    ConvertJobs jobs{};
+    auto add = [&](const float* src, void* dst, long long n) {
+      if (dst && n > 0) { jobs.src[jobs.n] = src; jobs.dst[jobs.n] = dst; jobs.count[jobs.n] = n; ++jobs.n; }
+    };
+    add(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo);
+    if (g.use_mask) add(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo);
+    add(gw32, gw, (long long)g.Co * g.Cig * g.T);
+    add(gb32, gb, (long long)g.Co);
+    if (jobs.n > 0) {
+      KernelScope ks("f32_convert_multi", st);
+      convert_multi_kernel<T><<<148 * 4, 256, 0, st>>>(jobs);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+  }
   return cudaSuccess;
 }
 
