@@ -422,9 +422,13 @@ struct DgradArgs {
 // Row strides of 20 and 36 words keep the 16-byte accesses aligned and
 // spread over the banks.
 struct DgWarpSmem {
-  float slab[32][20];
+  float slab[32][16];    // 16-byte chunk k of row r stored at chunk k ^ ((r >> 1) & 3)
   uint32_t tab[32][36];
 };
+
+// Chunk position in a slab row: conflict-free both for the row owner's
+// 16-byte stores (8 rows per phase) and for the 4-lanes-per-row loads.
+__device__ __forceinline__ int slab_pos(int r, int k) { return (k ^ ((r >> 1) & 3)) * 4; }
 
 // Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
 // streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each;
@@ -519,6 +523,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       kw.start(g, kc_lo + i);
       const int cbase = grp * g.Cig + kw.cc * BK;
       int coord_o = -1, acc_o = -1;
+      int tab_o[2] = {-1, -1};   // offset group currently in each table slot
       float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
       // coordinates of the row owner's sample for offset group coord_o
       int cidx[4] = {0, 0, 0, 0};
@@ -548,12 +553,16 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         float* srow = ws->slab[lane];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          *reinterpret_cast<uint4*>(srow + 4 * k) = make_uint4(acc[4 * k], acc[4 * k + 1], acc[4 * k + 2], acc[4 * k + 3]);
+          *reinterpret_cast<uint4*>(srow + slab_pos(lane, k)) =
+              make_uint4(acc[4 * k], acc[4 * k + 1], acc[4 * k + 2], acc[4 * k + 3]);
         int slot_o[2];
 #pragma unroll
         for (int sg = 0; sg < 2; ++sg) {
           const int o = (cbase + sl * 16 + sg * 8) / g.cpo;
           slot_o[sg] = o;
+          // the table slot already holds this offset group's sample (same K chunk)
+          if (sl > 0 && o == tab_o[sg]) continue;
+          tab_o[sg] = o;
           if (o != coord_o) {
             coord_o = o;
             const RawSample<T> raw = load_raw(g, off, msk, pc, o, kw.t);
@@ -589,7 +598,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           const uint4 tb = *reinterpret_cast<const uint4*>(tr);
           const uint4 tw = *reinterpret_cast<const uint4*>(tr + 4);
           const uint4 tx = *reinterpret_cast<const uint4*>(tr + 8);
-          const float4 gv = *reinterpret_cast<const float4*>(ws->slab[rr] + qq * 4);
+          const float4 gv = *reinterpret_cast<const float4*>(ws->slab[rr] + slab_pos(rr, qq));
           const int c_abs = cbase + sl * 16 + qq * 4;
           const int ci[4] = {(int)tb.x, (int)tb.y, (int)tb.z, (int)tb.w};
           const float w[4] = {__uint_as_float(tw.x), __uint_as_float(tw.y), __uint_as_float(tw.z),
@@ -812,11 +821,25 @@ struct ConvertJobs {
 template <typename T>
 __global__ void convert_multi_kernel(const ConvertJobs jobs) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   for (int j = 0; j < jobs.n; ++j) {
     const float* __restrict__ s = jobs.src[j];
     T* __restrict__ d = static_cast<T*>(jobs.dst[j]);
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < jobs.count[j]; e += stride)
-      d[e] = from_f<T>(s[e]);
+    const long long n = jobs.count[j];
+    // 4 elements per step when both ends are aligned (workspace is; outputs from
+    // the caching allocator are), scalar otherwise and for the tail
+    const bool vec = ((reinterpret_cast<uintptr_t>(d) & 7) == 0) && ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
+    const long long n4 = vec ? n / 4 : 0;
+    for (long long e = tid; e < n4; e += stride) {
+      const float4 v = reinterpret_cast<const float4*>(s)[e];
+      typename Packed<T>::P2 lo, hi;
+      lo.x = from_f<T>(v.x); lo.y = from_f<T>(v.y); hi.x = from_f<T>(v.z); hi.y = from_f<T>(v.w);
+      uint2 o;
+      o.x = *reinterpret_cast<uint32_t*>(&lo);
+      o.y = *reinterpret_cast<uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(d)[e] = o;
+    }
+    for (long long e = n4 * 4 + tid; e < n; e += stride) d[e] = from_f<T>(s[e]);
   }
 }
 
@@ -998,7 +1021,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     add(gb32, gb, (long long)g.Co);
     if (jobs.n > 0) {
       KernelScope ks("f32_convert_multi", st);
-      convert_multi_kernel<T><<<148 * 4, 256, 0, st>>>(jobs);
+      convert_multi_kernel<T><<<148 * 16, 256, 0, st>>>(jobs);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
   }
