@@ -56,3 +56,20 @@ def test_modules_and_state_dict_names():
     assert set(mm.state_dict()) == {"weight", "bias", "offset_conv.weight", "offset_conv.bias"}
     assert mm.offset_conv.out_channels == 3 * 9 * 2
     assert torch.count_nonzero(mm.offset_conv.weight) == 0
+
+
+def test_torchvision_registration_keeps_cpu_kernels():
+    """Registering the CUDA implementations leaves torchvision's CPU path intact."""
+    import numpy as np
+    from torchvision.ops import deform_conv2d as tv
+    from mps_deform_conv.torchvision_ops import register_torchvision_ops, registered
+    from oracle import oracle
+    register_torchvision_ops()
+    register_torchvision_ops()  # idempotent
+    assert registered()
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(1, 4, 6, 6, generator=g, dtype=torch.float64)
+    w = torch.randn(3, 4, 3, 3, generator=g, dtype=torch.float64)
+    off = torch.randn(1, 18, 6, 6, generator=g, dtype=torch.float64)
+    out = tv(x, off, w, padding=(1, 1))
+    np.testing.assert_allclose(out.numpy(), oracle.forward(x, off, w, None, 1, 1, 1, None), rtol=1e-12, atol=1e-12)
