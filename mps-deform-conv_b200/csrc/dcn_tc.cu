@@ -23,6 +23,7 @@
 // the device status word and unwinds.
 #include <type_traits>
 
+#include "dcn_layout.cuh"
 #include "dcn_tc_common.cuh"
 
 namespace dcn {
@@ -256,26 +257,23 @@ __global__ void nchw_to_nhwc_kernel(const T* __restrict__ x, T* __restrict__ xh,
 }
 
 // weight [Co][Cig][T] -> [G][NKC][Cog][64], K chunk kc = (cc, t) with t
-// fastest, rows 128-byte swizzled (chunk j of row co at j ^ (co % 8)).
+// fastest, rows 128-byte swizzled (chunk q of row co at q ^ (co % 8)).
+// blockIdx.x = grp * nkc + kc; a thread gathers the 8 channels of one 16-byte
+// chunk and stores it whole.
 template <typename T>
-__global__ void weight_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wsw, int G, int Cog,
-                                      int Cig, int T_) {
-  const int nkc = (Cig / BK) * T_;
-  const long long total = (long long)G * nkc * Cog * BK;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(e % BK);
-    long long r = e / BK;
-    const int co = (int)(r % Cog);
-    r /= Cog;
-    const int kc = (int)(r % nkc);
-    const int grp = (int)(r / nkc);
-    const int t = kc % T_, cc = kc / T_;
-    const int c = cc * BK + j;
-    const T v = w[((long long)(grp * Cog + co) * Cig + c) * T_ + t];
-    const long long blk = ((long long)grp * nkc + kc) * Cog * BK;
-    wsw[blk + (long long)co * BK + (((j >> 3) ^ (co & 7)) << 3) + (j & 7)] = v;
-  }
+__global__ void weight_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wsw, int Cog, int Cig,
+                                      int T_, int nkc) {
+  const int grp = blockIdx.x / nkc, kc = blockIdx.x - grp * nkc;
+  const int t = kc % T_, cc = kc / T_;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;  // (co, chunk q)
+  if (i >= Cog * 8) return;
+  const int co = i >> 3, q = i & 7;
+  const T* src = w + ((long long)(grp * Cog + co) * Cig + cc * BK + q * 8) * T_ + t;
+  __align__(16) T buf[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) buf[k] = src[(long long)k * T_];
+  T* dst = wsw + (long long)blockIdx.x * Cog * BK + co * BK + ((q ^ (co & 7)) << 3);
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(buf);
 }
 
 // Pipeline depth: as many stages (<= 4) as fit one CTA per SM (the kernel's
@@ -374,16 +372,19 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   cudaError_t e;
   {
     KernelScope ks("nchw_to_nhwc", st);
-    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
-    nchw_to_nhwc_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
+    const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
+    if (layout::to_channels_last_vec_ok(x, xh, g.C, (long long)g.H * g.W))
+      layout::to_channels_last16_kernel<T, false><<<grid, layout::LAYOUT_THREADS, 0, st>>>(
+          x, xh, nullptr, g.C, g.H * g.W);
+    else
+      nchw_to_nhwc_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   {
     KernelScope ks("weight_swizzle", st);
-    const long long total = (long long)g.Co * g.Cig * g.T;
-    int blocks = (int)((total + 255) / 256);
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    weight_swizzle_kernel<T><<<blocks, 256, 0, st>>>(w, wsw, g.G, g.Cog, g.Cig, g.T);
+    const int nkc = (g.Cig / BK) * g.T;
+    const dim3 grid((unsigned)(g.G * nkc), (unsigned)((g.Cog * 8 + 255) / 256));
+    weight_swizzle_kernel<T><<<grid, 256, 0, st>>>(w, wsw, g.Cog, g.Cig, g.T, nkc);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 

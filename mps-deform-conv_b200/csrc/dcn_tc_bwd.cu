@@ -23,6 +23,7 @@
 //   finalize    fp32 accumulators -> caller dtype / NCHW.
 #include <cmath>
 
+#include "dcn_layout.cuh"
 #include "dcn_tc_common.cuh"
 
 namespace dcn {
@@ -745,29 +746,27 @@ __global__ void go_transpose_bias_kernel(const T* __restrict__ go, T* __restrict
 }
 
 // weight [Co][Cig][T] -> W^T tiles [G][NKC][KB][64 ch][64 co]: row = channel j
-// of K chunk kc = (cc, t), 64 output channels per 128-byte row, chunk
-// ((co % 64) / 8) of row j stored at position ^ (j % 8); co >= Cog are zero.
+// of K chunk kc = (cc, t), 64 output channels per 128-byte row, chunk q
+// (output channels 8q .. 8q+7 of the block) of row j stored at q ^ (j % 8);
+// co >= Cog are zero.  blockIdx.x = grp * nkc + kc, blockIdx.y = kb; a thread
+// gathers one 16-byte chunk and stores it whole.
 template <typename T>
-__global__ void weight_t_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wdt, int G, int Cog,
-                                        int Cig, int T_, int KB) {
-  const int nkc = (Cig / BK) * T_;
-  const long long total = (long long)G * nkc * KB * 64 * 64;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int col = (int)(e % 64);          // output channel within block (logical)
-    long long r = e / 64;
-    const int j = (int)(r % 64);            // channel within K chunk
-    r /= 64;
-    const int kb = (int)(r % KB);
-    r /= KB;
-    const int kc = (int)(r % nkc);
-    const int grp = (int)(r / nkc);
-    const int co = kb * 64 + col;
-    const int t = kc % T_, cc = kc / T_;
+__global__ void weight_t_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wdt, int Cog, int Cig,
+                                        int T_, int nkc) {
+  const int grp = blockIdx.x / nkc, kc = blockIdx.x - grp * nkc;
+  const int t = kc % T_, cc = kc / T_;
+  const int kb = blockIdx.y;
+  T* blk = wdt + ((long long)blockIdx.x * gridDim.y + kb) * 4096;
+  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+    const int j = i >> 3, q = i & 7;
     const int c = cc * BK + j;
-    const T v = co < Cog ? w[((long long)(grp * Cog + co) * Cig + c) * T_ + t] : from_f<T>(0.f);
-    const long long blk = (((long long)grp * nkc + kc) * KB + kb) * 4096;
-    wdt[blk + j * 64 + (((col >> 3) ^ (j & 7)) << 3) + (col & 7)] = v;
+    __align__(16) T buf[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int co = kb * 64 + q * 8 + k;
+      buf[k] = co < Cog ? w[((long long)(grp * Cog + co) * Cig + c) * T_ + t] : from_f<T>(0.f);
+    }
+    *reinterpret_cast<uint4*>(blk + j * 64 + ((q ^ (j & 7)) << 3)) = *reinterpret_cast<const uint4*>(buf);
   }
 }
 
@@ -822,7 +821,9 @@ template <typename T>
 __global__ void convert_multi_kernel(const ConvertJobs jobs) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  for (int j = 0; j < jobs.n; ++j) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= jobs.n) break;
     const float* __restrict__ s = jobs.src[j];
     T* __restrict__ d = static_cast<T*>(jobs.dst[j]);
     const long long n = jobs.count[j];
@@ -830,14 +831,20 @@ __global__ void convert_multi_kernel(const ConvertJobs jobs) {
     // the caching allocator are), scalar otherwise and for the tail
     const bool vec = ((reinterpret_cast<uintptr_t>(d) & 7) == 0) && ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
     const long long n4 = vec ? n / 4 : 0;
-    for (long long e = tid; e < n4; e += stride) {
-      const float4 v = reinterpret_cast<const float4*>(s)[e];
-      typename Packed<T>::P2 lo, hi;
-      lo.x = from_f<T>(v.x); lo.y = from_f<T>(v.y); hi.x = from_f<T>(v.z); hi.y = from_f<T>(v.w);
-      uint2 o;
-      o.x = *reinterpret_cast<uint32_t*>(&lo);
-      o.y = *reinterpret_cast<uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(d)[e] = o;
+    const float4* __restrict__ s4 = reinterpret_cast<const float4*>(s);
+    uint2* __restrict__ d4 = reinterpret_cast<uint2*>(d);
+    long long e = tid;
+    for (; e + 3 * stride < n4; e += 4 * stride) {  // 4 independent loads in flight
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = s4[e + k * stride];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        d4[e + k * stride] = make_uint2(Vec<T>::pack(v[k].x, v[k].y), Vec<T>::pack(v[k].z, v[k].w));
+    }
+    for (; e < n4; e += stride) {
+      const float4 v = s4[e];
+      d4[e] = make_uint2(Vec<T>::pack(v.x, v.y), Vec<T>::pack(v.z, v.w));
     }
     for (long long e = n4 * 4 + tid; e < n; e += stride) d[e] = from_f<T>(s[e]);
   }
@@ -872,11 +879,6 @@ uint32_t pow2_cols(int n) {
   return c;
 }
 
-static int grid_cap(long long n) {
-  long long b = (n + 255) / 256;
-  return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
-}
-
 template <typename T>
 cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, const T* off, const T* msk,
                           const void* saved, T* gin, T* gw, T* goff, T* gmsk, T* gb, void* workspace,
@@ -906,14 +908,23 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   if ((e = cudaMemsetAsync(ws + L.acc, 0, L.acc_bytes, st)) != cudaSuccess) return e;
   {
     KernelScope ks("go_transpose_bias", st);
-    dim3 grid((g.HWo + 63) / 64, (g.Co + 63) / 64, g.B);
-    go_transpose_bias_kernel<T><<<grid, 256, 0, st>>>(go, got, gb ? gb32 : nullptr, g.Co, g.HWo);
+    const dim3 grid = layout::tile_grid(g.Co, g.HWo, g.B);
+    if (!layout::to_channels_last_vec_ok(go, got, g.Co, g.HWo))
+      go_transpose_bias_kernel<T><<<grid, 256, 0, st>>>(go, got, gb ? gb32 : nullptr, g.Co, g.HWo);
+    else if (gb)
+      layout::to_channels_last16_kernel<T, true><<<grid, layout::LAYOUT_THREADS, 0, st>>>(go, got, gb32, g.Co, g.HWo);
+    else
+      layout::to_channels_last16_kernel<T, false><<<grid, layout::LAYOUT_THREADS, 0, st>>>(go, got, nullptr, g.Co, g.HWo);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (!saved) {  // channels-last input copy, unless the forward left one
     KernelScope ks("nchw_to_nhwc", st);
-    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
-    nchw_to_nhwc_bwd_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
+    const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
+    if (layout::to_channels_last_vec_ok(x, xh, g.C, (long long)g.H * g.W))
+      layout::to_channels_last16_kernel<T, false><<<grid, layout::LAYOUT_THREADS, 0, st>>>(
+          x, xh, nullptr, g.C, g.H * g.W);
+    else
+      nchw_to_nhwc_bwd_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
@@ -923,8 +934,8 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   if (need_d) {
     {
       KernelScope ks("weight_t_swizzle", st);
-      weight_t_swizzle_kernel<T><<<grid_cap((long long)g.G * nkc * KB * 4096), 256, 0, st>>>(
-          w, wdt, g.G, g.Cog, g.Cig, g.T, KB);
+      weight_t_swizzle_kernel<T><<<dim3((unsigned)(g.G * nkc), (unsigned)KB), 256, 0, st>>>(
+          w, wdt, g.Cog, g.Cig, g.T, nkc);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     DgradArgs a;
@@ -1006,8 +1017,12 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   // ---- finalize
   if (gin) {
     KernelScope ks("grad_input_to_nchw", st);
-    dim3 grid((g.H * g.W + 63) / 64, (g.C + 63) / 64, g.B);
-    nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
+    const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
+    if (layout::from_channels_last_vec_ok(gi32, gin, g.C, (long long)g.H * g.W))
+      layout::from_channels_last_f32_16_kernel<T><<<grid, layout::LAYOUT_THREADS, 0, st>>>(
+          gi32, gin, g.C, g.H * g.W);
+    else
+      nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {  // offset / mask / weight / bias gradients: fp32 -> T in one launch

@@ -103,6 +103,38 @@ def test_tc_forward_deterministic_and_batch_consistent(cuda):
     assert torch.equal(a[1:], c)
 
 
+def _at_2_byte_offset(t):
+    """The same values at a data pointer 2 bytes past a 4-byte boundary."""
+    buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+    v = buf[1:].view(t.shape)
+    v.copy_(t)
+    assert v.data_ptr() % 4 == 2
+    return v
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+def test_tc_layout_passes_unaligned_pointers(dtype, cuda):
+    """The vectorized NCHW <-> channels-last passes need 4/16-byte aligned
+    tensors; input and grad_output at a 2-byte offset take the scalar passes
+    and give the same results (forward bitwise; gradients, accumulated with
+    atomics in any order, within 1e-3)."""
+    from mps_deform_conv import _abi
+    T = _make(SHAPES["c128_g2_og4_dil2"], DTYPES[dtype], cuda, seed=21)  # 10x10 planes: vectorized when aligned
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    x_u, go_u = _at_2_byte_offset(T["input"]), _at_2_byte_offset(T["grad_output"])
+    a = _abi.call_forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    u = _abi.call_forward(x_u, T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    ga = _abi.call_backward(T["grad_output"], T["input"], T["offset"], T["weight"], st, pd, dl, T["mask"],
+                            with_bias=True)
+    gu = _abi.call_backward(go_u, x_u, T["offset"], T["weight"], st, pd, dl, T["mask"], with_bias=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a, u)
+    for name, p, q in zip(("input", "offset", "weight", "bias", "mask"), ga, gu):
+        assert rel_err(to_np(q), to_np(p)) <= 1e-3, name
+    ref = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
+    assert rel_err(to_np(u), ref) <= TOL[dtype]
+
+
 @pytest.mark.parametrize("mask_sel", [(1, 0, 0, 0, 0), (0, 1, 0, 0, 1), (0, 0, 1, 1, 0)])
 def test_tc_backward_output_subsets(mask_sel, cuda):
     """Only the requested gradients are computed and they match the full call."""
