@@ -31,7 +31,7 @@ sys.path.insert(0, REPO)
 
 import torch  # noqa: E402
 
-from mps_deform_conv.sharding import allreduce_param_grads, shard_range  # noqa: E402
+from mps_deform_conv.sharding import OverlappedParamAllReduce, allreduce_param_grads, shard_range  # noqa: E402
 from mps_deform_conv.workloads import PROBLEMS, make_inputs  # noqa: E402
 
 METRIC = "deform_conv2d fwd+bwd TFLOP/s & % roofline per B200; samples/s at 1/2/4/8 GPUs"
@@ -237,8 +237,18 @@ def run_ours(args):
             t.requires_grad_(True)
     param_grads_idx = [2] + ([3] if b is not None else [])
 
+    # grad_weight and grad_bias sum over the global batch: one flat-bucket
+    # all-reduce per step, started from the backward's parameter-gradient hook
+    # on a side stream (it overlaps the input/offset/mask gradient kernels),
+    # or after the backward with --no-overlap
+    overlap = world > 1 and p.training and not args.no_overlap
+    ar = OverlappedParamAllReduce() if overlap else None
+    mdc.set_param_grad_hook(ar)
+
     def reduce_grads(grads):
-        if world > 1:  # grad_weight and grad_bias sum over the global batch
+        if ar is not None:
+            ar.wait()
+        elif world > 1:
             allreduce_param_grads([grads[i] for i in range(len(grads)) if leaves[i] is w or leaves[i] is b])
 
     fwd_ev = []
@@ -379,7 +389,10 @@ def run_ours(args):
             "data": "synthetic (seeded; workload distributions)",
             "config": {"workload": p.name, "description": p.description, "global_batch": p.batch,
                        "per_gpu_batch": nb, "parallelism": f"batch-sharded dp{world}" + (
-                           ", grad_weight/grad_bias NCCL all-reduce" if world > 1 and p.training else ""),
+                           (", grad_weight/grad_bias NCCL all-reduce on a side stream, overlapping the "
+                            "input/offset/mask gradients" if overlap else
+                            ", grad_weight/grad_bias NCCL all-reduce after the backward")
+                           if world > 1 and p.training else ""),
                        "l2": "flushed between steps (256 MB write)" if flush is not None
                        else f"inputs {in_bytes / 2**20:.0f} MB per rank > L2",
                        "fwd_ms_per_step": round(sum(fwd_ms) / args.steps, 4)},
@@ -536,7 +549,9 @@ def run_e2e(p, inp, args, dev, world):
             lv = [t for t in (x, off, dev_w, dev_b, m) if t is not None]
             grads = torch.autograd.grad(out, lv, b["grad_output"])
             res = [grads[2]] + ([grads[3]] if dev_b is not None else [])
-            if world > 1:
+            if isinstance(mdc._param_grad_hook, OverlappedParamAllReduce):
+                mdc._param_grad_hook.wait()
+            elif world > 1:
                 allreduce_param_grads(res)
         else:
             res = [out]
@@ -594,6 +609,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-suite", action="store_true", help="skip the short runs of the other workloads")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of a CUDA graph")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="all-reduce the parameter gradients after the backward instead of during it")
     ap.add_argument("--traffic-per-launch", type=float, default=None,
                     help="ncu dram bytes per launch of the dominant kernel, if captured")
     args = ap.parse_args()

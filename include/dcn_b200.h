@@ -210,6 +210,35 @@ DCN_API int dcn_deform_conv2d_backward_train(const dcn_conv_desc *desc, const vo
                                              void *stream);
 
 /* ---------------------------------------------------------------------
+ * Backward with a parameter-gradient callback, for overlapping the
+ * data-parallel all-reduce of grad_weight / grad_bias with the rest of the
+ * backward.  No reference counterpart: the reference's backward
+ * (mps_deform_conv/__init__.py:245-322) returns all gradients at once and
+ * its caller reduces them afterwards.
+ *
+ * Same arguments and results as dcn_deform_conv2d_backward_train (`saved`
+ * may be NULL).  `params_ready(user_data)` is called exactly once, on the
+ * calling thread, after every kernel that writes grad_weight and grad_bias
+ * has been enqueued on `stream`: work that the callback enqueues on another
+ * stream after waiting on an event it records on `stream` sees the final
+ * parameter gradients.  On the tensor-core path the callback comes before
+ * the input / offset / mask gradient kernels are enqueued, so that work runs
+ * alongside them; on the other paths it comes after them.  It is not called
+ * when the function returns an error before enqueuing anything.  The callback
+ * must not call back into this library on the same stream.
+ */
+typedef void (*dcn_params_ready_fn)(void *user_data);
+DCN_API int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc *desc, const void *grad_output,
+                                               const void *input, const void *weight,
+                                               const void *offset, const void *mask,
+                                               const void *saved, size_t saved_bytes,
+                                               void *grad_input, void *grad_weight,
+                                               void *grad_offset, void *grad_mask,
+                                               void *grad_bias, void *workspace,
+                                               size_t workspace_bytes, void *stream,
+                                               dcn_params_ready_fn params_ready, void *user_data);
+
+/* ---------------------------------------------------------------------
  * Device status.  Kernels with bounded waits record an expired wait in a
  * device-side status word instead of hanging.  This call copies and clears
  * it (it synchronises `stream`): DCN_OK, or DCN_ERR_DEVICE_TIMEOUT.

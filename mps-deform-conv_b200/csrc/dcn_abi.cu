@@ -408,11 +408,14 @@ size_t dcn_backward_workspace_size(const dcn_conv_desc* d) {
   return simt_bwd_layout(d, g).total;
 }
 
+// `ready(user)`, when given, is called once the grad_weight / grad_bias
+// kernels are enqueued (dcn_deform_conv2d_backward_overlap).
 static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const void* input,
                          const void* weight, const void* offset, const void* mask,
                          const void* saved, size_t saved_bytes, void* grad_input,
                          void* grad_weight, void* grad_offset, void* grad_mask, void* grad_bias,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+                         void* workspace, size_t workspace_bytes, void* stream,
+                         dcn_params_ready_fn ready = nullptr, void* user = nullptr) {
   int r = validate(d);
   if (r != DCN_OK) return r;
   const Geom g = make_geom(*d);
@@ -423,6 +426,7 @@ static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const 
     const size_t es = elem_size(d->dtype);
     if (grad_weight) e = cudaMemsetAsync(grad_weight, 0, es * (size_t)g.Co * g.Cig * g.T, st);
     if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, es * (size_t)g.Co, st);
+    if (e == cudaSuccess && ready) ready(user);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
   }
   if (!grad_output || !input || !weight || !offset || (d->use_mask && !mask))
@@ -437,7 +441,7 @@ static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const 
       return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
                   saved_bytes);
     cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset, mask, saved, grad_input,
-                                grad_weight, grad_offset, grad_mask, grad_bias, workspace, st);
+                                grad_weight, grad_offset, grad_mask, grad_bias, workspace, st, ready, user);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward (tensor core)");
   }
   const SimtBwdLayout L = simt_bwd_layout(d, g);
@@ -459,6 +463,7 @@ static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const 
                          (T*)grad_weight, (T*)grad_offset, (T*)grad_mask, (T*)grad_bias, ws, st);
     return 0;
   });
+  if (e == cudaSuccess && ready) ready(user);
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward");
 }
 
@@ -482,6 +487,20 @@ int dcn_deform_conv2d_backward_train(const dcn_conv_desc* d, const void* grad_ou
   return backward_impl(d, grad_output, input, weight, offset, mask, saved, saved_bytes, grad_input,
                        grad_weight, grad_offset, grad_mask, grad_bias, workspace, workspace_bytes,
                        stream);
+}
+
+int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc* d, const void* grad_output,
+                                       const void* input, const void* weight, const void* offset,
+                                       const void* mask, const void* saved, size_t saved_bytes,
+                                       void* grad_input, void* grad_weight, void* grad_offset,
+                                       void* grad_mask, void* grad_bias, void* workspace,
+                                       size_t workspace_bytes, void* stream, dcn_params_ready_fn params_ready,
+                                       void* user_data) {
+  if (validate(d) != DCN_OK) return validate(d);
+  if (dcn_saved_state_bytes(d) == 0) saved = nullptr;
+  return backward_impl(d, grad_output, input, weight, offset, mask, saved, saved_bytes, grad_input,
+                       grad_weight, grad_offset, grad_mask, grad_bias, workspace, workspace_bytes,
+                       stream, params_ready, user_data);
 }
 
 int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void* grad_col,

@@ -31,7 +31,8 @@ cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input,
 cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output,
                         const void* input, const void* weight, const void* offset, const void* mask,
                         const void* saved, void* grad_input, void* grad_weight, void* grad_offset,
-                        void* grad_mask, void* grad_bias, void* workspace, cudaStream_t st);
+                        void* grad_mask, void* grad_bias, void* workspace, cudaStream_t st,
+                        dcn_params_ready_fn ready, void* user);
 // Copies the device status word (non-zero after an expired bounded wait)
 // into *out and clears it; synchronises the stream.
 cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st);

@@ -46,7 +46,7 @@ struct WgradArgs {
   const void* xh;
   const void* off;
   const void* msk;
-  float* gw32;     // [Co][Cig][T] fp32, zeroed
+  float* gwp;      // per-split partial gW [splits][Co][nkc][64] fp32 (kc = cc*T + t)
   int* status;
   Geom g;
   int nkc;         // K chunks per group, kc = cc*T + t
@@ -59,6 +59,20 @@ struct WgradArgs {
   uint32_t idesc;
   uint32_t tmem_cols;
 };
+
+// One 16-column TMEM load of the gW accumulator (row co, channels c16*16 ..
+// c16*16+15 of K chunk kc) into this CTA's split of the partial buffer: plain
+// 16-byte stores, every element written by exactly one CTA.
+__device__ __forceinline__ void store_wgrad_partial(const WgradArgs& a, int co, int kc, int c16,
+                                                    const uint32_t (&v)[16]) {
+  const Geom& g = a.g;
+  float4* dst = reinterpret_cast<float4*>(
+      a.gwp + ((((size_t)blockIdx.z * g.Co + (size_t)blockIdx.y * g.Cog + co) * a.nkc + kc) * 64 + c16 * 16));
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                         __uint_as_float(v[4 * i + 3]));
+}
 
 struct WgradSmem {
   uint32_t a, a_stage, b, bar, total;
@@ -137,7 +151,7 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
                            fb = b_full(s);
                          });
     }
-    // -------------------------------------------- epilogue: TMEM -> fp32 atomics
+    // -------------------------------------------- epilogue: TMEM -> this split's partial gW
     const bool ready = nt > 0 && ok && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
     if (__all_sync(0xffffffffu, ready)) {
       tc_fence_after();
@@ -145,19 +159,13 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
       for (int blk = quarter; blk < a.mh * nk; blk += W_NPROD_WARPS / 4) {
         const int h = blk / nk, kcl = blk % nk;
         const int co = h * BM + q * 32 + lane;
-        const int kc = k0 + kcl;
-        const int t = kc % g.T, cc = kc / g.T;
         const uint32_t col = (uint32_t)((h * a.nkg + kcl) * 64);
 #pragma unroll 1
         for (int c16 = 0; c16 < 4; ++c16) {
           uint32_t v[16];
           tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + col + c16 * 16, v);
           tmem_ld_wait();
-          if (co < g.Cog) {
-            float* dst = a.gw32 + ((long long)(grp * g.Cog + co) * g.Cig + cc * BK + c16 * 16) * g.T + t;
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) atomicAdd(dst + (long long)jj * g.T, __uint_as_float(v[jj]));
-          }
+          if (co < g.Cog) store_wgrad_partial(a, co, k0 + kcl, c16, v);
         }
       }
     }
@@ -298,7 +306,7 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
   const uint32_t tmem = *tmem_slot;
 
   if (warp < WC_EPI_WARPS) {
-    // -------------------------------------------- epilogue: TMEM -> fp32 atomics
+    // -------------------------------------------- epilogue: TMEM -> this split's partial gW
     const bool ready = nslices > 0 && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
     if (__all_sync(0xffffffffu, ready)) {
       tc_fence_after();
@@ -306,19 +314,13 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
       for (int blk = 0; blk < a.mh * nk; ++blk) {
         const int h = blk / nk, kcl = blk % nk;
         const int co = h * BM + q * 32 + lane;
-        const int kc = k0 + kcl;
-        const int t = kc % g.T, cc = kc / g.T;
         const uint32_t col = (uint32_t)(h * a.nkg * 64 + kcl * 64);
 #pragma unroll 1
         for (int c16 = 0; c16 < 4; ++c16) {
           uint32_t v[16];
           tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + col + c16 * 16, v);
           tmem_ld_wait();
-          if (co < g.Cog) {
-            float* dst = a.gw32 + ((long long)(grp * g.Cog + co) * g.Cig + cc * BK + c16 * 16) * g.T + t;
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) atomicAdd(dst + (long long)jj * g.T, __uint_as_float(v[jj]));
-          }
+          if (co < g.Cog) store_wgrad_partial(a, co, k0 + kcl, c16, v);
         }
       }
     }
@@ -850,9 +852,72 @@ __global__ void convert_multi_kernel(const ConvertJobs jobs) {
   }
 }
 
+// gW [Co][Cig][T] = sum over splits (in split order) of the partials
+// [splits][Co][nkc][64], and gB = gb32 in T when gb is given.  One CTA per
+// (output channel, 64-channel block cc):
+// the 64*T partials of one split are one contiguous run [t][j] (kc = cc*T + t),
+// read as float4 and summed in registers; a padded shared-memory tile turns
+// them into the contiguous output run [j][t].  Dynamic shared memory:
+// T * 65 floats.
+constexpr int WR_THREADS = 128;
+inline size_t wgrad_reduce_smem(int T_) { return sizeof(float) * (size_t)T_ * 65; }
+
+template <typename T>
+__global__ void __launch_bounds__(WR_THREADS)
+wgrad_reduce_kernel(const float* __restrict__ gwp, T* __restrict__ gw, const float* __restrict__ gb32,
+                    T* __restrict__ gb, int splits, int Co, int Cig, int T_) {
+  extern __shared__ float wr_tile[];  // [T][65]
+  if (gb && blockIdx.x == 0)  // the bias gradient rides along: fp32 sums -> T
+    for (int i = threadIdx.x; i < Co; i += WR_THREADS) gb[i] = from_f<T>(gb32[i]);
+  const int ncc = Cig / BK;
+  const int co = blockIdx.x / ncc, cc = blockIdx.x - co * ncc;
+  const int nkc = ncc * T_;
+  const size_t split_stride4 = (size_t)Co * nkc * 16;
+  const float4* src = reinterpret_cast<const float4*>(gwp + ((size_t)co * nkc + (size_t)cc * T_) * 64);
+  for (int i = threadIdx.x; i < 16 * T_; i += WR_THREADS) {
+    float4 acc = src[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = src[sp * split_stride4 + i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float* row = wr_tile + (i >> 4) * 65 + (i & 15) * 4;
+    row[0] = acc.x; row[1] = acc.y; row[2] = acc.z; row[3] = acc.w;
+  }
+  __syncthreads();
+  T* dst = gw + ((size_t)co * Cig + (size_t)cc * BK) * T_;
+  for (int e = threadIdx.x; e < BK * T_; e += WR_THREADS) {
+    const int j = e / T_, t = e - j * T_;
+    dst[e] = from_f<T>(wr_tile[t * 65 + j]);
+  }
+}
+
 // ================================================================ host
+// Work split of the weight-gradient GEMM: CTAs own nkg K chunks (TMEM holds
+// mh * nkg * 64 fp32 columns <= 512) of one group and a contiguous range of
+// pixel tiles; about one wave of CTAs (one CTA per SM), at least 4 tiles each.
+struct WgradPlan {
+  int mh, nkg, ncb, kgroups, splits, tiles_per_cta, n_tiles;
+};
+WgradPlan wgrad_plan(const Geom& g) {
+  WgradPlan w;
+  const int nkc = (g.Cig / BK) * g.T;
+  w.n_tiles = (int)((g.P + BM - 1) / BM);
+  w.mh = (g.Cog + BM - 1) / BM;
+  const int nkg_max = 8 / w.mh;
+  const int ngroups = (nkc + nkg_max - 1) / nkg_max;
+  w.nkg = (nkc + ngroups - 1) / ngroups;
+  w.ncb = (g.Cog + 63) / 64;
+  w.kgroups = (nkc + w.nkg - 1) / w.nkg;
+  int splits = 148 / (w.kgroups * g.G);
+  if (splits > w.n_tiles / 4) splits = w.n_tiles / 4;
+  if (splits < 1) splits = 1;
+  w.tiles_per_cta = w.n_tiles > 0 ? (w.n_tiles + splits - 1) / splits : 1;
+  w.splits = w.n_tiles > 0 ? (w.n_tiles + w.tiles_per_cta - 1) / w.tiles_per_cta : 1;
+  return w;
+}
+
 struct BwdWs {
-  size_t xh, got, wdt, acc, gi32, goff32, gmsk32, gw32, gb32, acc_bytes, total;
+  size_t xh, got, wdt, acc, gi32, goff32, gmsk32, gb32, acc_bytes, gwp, total;
 };
 BwdWs bwd_ws(const Geom& g, size_t es) {
   BwdWs L;
@@ -866,9 +931,10 @@ BwdWs bwd_ws(const Geom& g, size_t es) {
   L.gi32 = o;   o += ws_align(4 * (size_t)g.B * g.H * g.W * g.C);
   L.goff32 = o; o += ws_align(4 * (size_t)g.B * g.OG * 2 * g.T * g.HWo);
   L.gmsk32 = o; o += ws_align(4 * (size_t)g.B * g.OG * g.T * g.HWo);
-  L.gw32 = o;   o += ws_align(4 * (size_t)g.Co * g.Cig * g.T);
   L.gb32 = o;   o += ws_align(4 * (size_t)g.Co);
   L.acc_bytes = o - L.acc;
+  L.gwp = o;  // written whole by the wgrad kernels: not cleared
+  o += ws_align(4 * (size_t)wgrad_plan(g).splits * g.Co * g.Cig * g.T);
   L.total = o;
   return L;
 }
@@ -882,7 +948,7 @@ uint32_t pow2_cols(int n) {
 template <typename T>
 cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, const T* off, const T* msk,
                           const void* saved, T* gin, T* gw, T* goff, T* gmsk, T* gb, void* workspace,
-                          cudaStream_t st) {
+                          cudaStream_t st, dcn_params_ready_fn ready, void* user) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const BwdWs L = bwd_ws(g, sizeof(T));
   char* ws = static_cast<char*>(workspace);
@@ -895,7 +961,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   float* gi32 = reinterpret_cast<float*>(ws + L.gi32);
   float* goff32 = reinterpret_cast<float*>(ws + L.goff32);
   float* gmsk32 = reinterpret_cast<float*>(ws + L.gmsk32);
-  float* gw32 = reinterpret_cast<float*>(ws + L.gw32);
+  float* gwp = reinterpret_cast<float*>(ws + L.gwp);
   float* gb32 = reinterpret_cast<float*>(ws + L.gb32);
   int* status = tc_status_ptr();
   if (!status) return cudaErrorSymbolNotFound;
@@ -931,55 +997,16 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   CUtensorMap tmap;
   if (!make_tmap_2d(&tmap, got, bf16, (uint64_t)g.P, (uint64_t)g.Co, BM, 64)) return cudaErrorInvalidValue;
 
-  if (need_d) {
-    {
-      KernelScope ks("weight_t_swizzle", st);
-      weight_t_swizzle_kernel<T><<<dim3((unsigned)(g.G * nkc), (unsigned)KB), 256, 0, st>>>(
-          w, wdt, g.Cog, g.Cig, g.T, nkc);
-    }
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    DgradArgs a;
-    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.wdt = wdt;
-    a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
-    a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
-    a.b_stages = 4;
-    while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) --a.b_stages;
-    if (dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
-    a.idesc = idesc_f16(BM, 64, bf16);
-    const int smem = (int)dgrad_smem(KB, a.b_stages).total + 1024;
-    if ((e = cudaFuncSetAttribute(dcn_dgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
-      return e;
-    // split the K chunks of a tile over ksplit CTAs when that fills the last
-    // wave of 148 SMs (one CTA per SM) better; keep >= 4 chunks per CTA
-    int ksplit = 1;
-    double best = 0.0;
-    for (int k = 1; k <= 6 && nkc / k >= 4; ++k) {
-      const double waves = (double)n_tiles * g.G * k / 148.0;
-      const double eff = waves / std::ceil(waves);
-      if (eff > best + 0.05) { best = eff; ksplit = k; }
-    }
-    KernelScope ks("dcn_dgrad_tc", st);
-    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
   if (gw) {
     WgradArgs a;
-    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.gw32 = gw32;
+    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.gwp = gwp;
     a.status = status; a.g = g; a.nkc = nkc;
-    a.mh = (g.Cog + BM - 1) / BM;
-    const int nkg_max = 8 / a.mh;  // TMEM: mh * nkg * 64 columns <= 512
-    const int ngroups = (nkc + nkg_max - 1) / nkg_max;
-    a.nkg = (nkc + ngroups - 1) / ngroups;
-    a.ncb = (g.Cog + 63) / 64;
-    const int kgroups = (nkc + a.nkg - 1) / a.nkg;
-    // about one wave of CTAs: every CTA ends with an atomic add of its whole
-    // [Cog x nkg*64] partial, so more CTAs cost more atomics
-    const int base = kgroups * g.G;
-    int splits = 148 / base;
-    if (splits > n_tiles / 4) splits = n_tiles / 4;
-    if (splits < 1) splits = 1;
-    a.tiles_per_cta = (n_tiles + splits - 1) / splits;
-    splits = (n_tiles + a.tiles_per_cta - 1) / a.tiles_per_cta;
+    const WgradPlan wp = wgrad_plan(g);
+    a.mh = wp.mh;
+    a.nkg = wp.nkg;
+    a.ncb = wp.ncb;
+    const int kgroups = wp.kgroups, splits = wp.splits;
+    a.tiles_per_cta = wp.tiles_per_cta;
     a.n_tiles = n_tiles;
     a.b_stages = 4;
     a.a_stages = 2;
@@ -1013,6 +1040,59 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       dcn_wgrad_tc_kernel<T><<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    {
+      KernelScope ks("wgrad_reduce", st);
+      const size_t rsmem = wgrad_reduce_smem(g.T);
+      if (rsmem > 48 * 1024 &&
+          (e = cudaFuncSetAttribute(wgrad_reduce_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)rsmem)) != cudaSuccess)
+        return e;
+      wgrad_reduce_kernel<T><<<(unsigned)(g.Co * (g.Cig / BK)), WR_THREADS, rsmem, st>>>(
+          gwp, gw, gb ? gb32 : nullptr, gb, splits, g.Co, g.Cig, g.T);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+  }
+  if (gb && !gw) {  // bias gradient alone
+    ConvertJobs jobs{};
+    jobs.src[0] = gb32; jobs.dst[0] = gb; jobs.count[0] = g.Co; jobs.n = 1;
+    KernelScope ks("f32_convert_multi", st);
+    convert_multi_kernel<T><<<1, 256, 0, st>>>(jobs);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  // grad_weight and grad_bias are final once the work enqueued so far has run:
+  // a caller can start their all-reduce on another stream while the input /
+  // offset / mask gradients are computed below
+  if (ready) ready(user);
+  if (need_d) {
+    {
+      KernelScope ks("weight_t_swizzle", st);
+      weight_t_swizzle_kernel<T><<<dim3((unsigned)(g.G * nkc), (unsigned)KB), 256, 0, st>>>(
+          w, wdt, g.Cog, g.Cig, g.T, nkc);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    DgradArgs a;
+    a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.wdt = wdt;
+    a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
+    a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
+    a.b_stages = 4;
+    while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) --a.b_stages;
+    if (dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
+    a.idesc = idesc_f16(BM, 64, bf16);
+    const int smem = (int)dgrad_smem(KB, a.b_stages).total + 1024;
+    if ((e = cudaFuncSetAttribute(dcn_dgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      return e;
+    // split the K chunks of a tile over ksplit CTAs when that fills the last
+    // wave of 148 SMs (one CTA per SM) better; keep >= 4 chunks per CTA
+    int ksplit = 1;
+    double best = 0.0;
+    for (int k = 1; k <= 6 && nkc / k >= 4; ++k) {
+      const double waves = (double)n_tiles * g.G * k / 148.0;
+      const double eff = waves / std::ceil(waves);
+      if (eff > best + 0.05) { best = eff; ksplit = k; }
+    }
+    KernelScope ks("dcn_dgrad_tc", st);
+    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   // ---- finalize
   if (gin) {
@@ -1025,15 +1105,13 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  {  // offset / mask / weight / bias gradients: fp32 -> T in one launch
+  {  // offset / mask gradients: fp32 -> T in one launch
     ConvertJobs jobs{};
     auto add = [&](const float* src, void* dst, long long n) {
       if (dst && n > 0) { jobs.src[jobs.n] = src; jobs.dst[jobs.n] = dst; jobs.count[jobs.n] = n; ++jobs.n; }
     };
     add(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo);
     if (g.use_mask) add(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo);
-    add(gw32, gw, (long long)g.Co * g.Cig * g.T);
-    add(gb32, gb, (long long)g.Co);
     if (jobs.n > 0) {
       KernelScope ks("f32_convert_multi", st);
       convert_multi_kernel<T><<<148 * 16, 256, 0, st>>>(jobs);
@@ -1047,8 +1125,10 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
 
 bool tc_backward_supported(const dcn_conv_desc& d, const Geom& g) {
   // dgrad keeps the [128 px][C_out/group] grad_output tile resident next to
-  // the epilogue scratch: C_out/group <= 256; corner indices are 32-bit.
-  return tc_forward_supported(d, g) && g.Cog <= 256 && (long long)g.B * g.H * g.W < (1LL << 31);
+  // the epilogue scratch: C_out/group <= 256; corner indices are 32-bit; the
+  // gW reduction stages T*65 floats in shared memory.
+  return tc_forward_supported(d, g) && g.Cog <= 256 && (long long)g.B * g.H * g.W < (1LL << 31) &&
+         wgrad_reduce_smem(g.T) <= 227 * 1024;
 }
 
 size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g) {
@@ -1058,17 +1138,18 @@ size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g) {
 cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output, const void* input,
                         const void* weight, const void* offset, const void* mask, const void* saved,
                         void* grad_input, void* grad_weight, void* grad_offset, void* grad_mask,
-                        void* grad_bias, void* workspace, cudaStream_t st) {
+                        void* grad_bias, void* workspace, cudaStream_t st, dcn_params_ready_fn ready,
+                        void* user) {
   if (d.dtype == DCN_BFLOAT16) {
     using T = __nv_bfloat16;
     return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
                             (const T*)mask, saved, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
-                            (T*)grad_mask, (T*)grad_bias, workspace, st);
+                            (T*)grad_mask, (T*)grad_bias, workspace, st, ready, user);
   }
   using T = __half;
   return tc_backward_t<T>(g, (const T*)grad_output, (const T*)input, (const T*)weight, (const T*)offset,
                           (const T*)mask, saved, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
-                          (T*)grad_mask, (T*)grad_bias, workspace, st);
+                          (T*)grad_mask, (T*)grad_bias, workspace, st, ready, user);
 }
 
 }  // namespace dcn

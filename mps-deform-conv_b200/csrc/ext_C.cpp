@@ -11,6 +11,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <exception>
 #include <optional>
 #include <tuple>
 #include <vector>
@@ -268,7 +269,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
     const at::Tensor& offset, const at::Tensor& mask, const at::Tensor& bias, int64_t stride_h,
     int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
     int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask, std::vector<bool> output_mask,
-    const std::optional<at::Tensor>& saved_opt) {
+    const std::optional<at::Tensor>& saved_opt, const std::optional<py::function>& params_ready) {
   TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
   check_cuda(grad_output, "grad_output", input);
   check_cuda(weight, "weight", input);
@@ -306,10 +307,36 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
                     saved.is_contiguous(),
                 "saved state must be a contiguous uint8 tensor on the input's device");
   }
-  check_status(dcn_deform_conv2d_backward_train(
+  if (!params_ready.has_value() || params_ready->is_none()) {
+    check_status(dcn_deform_conv2d_backward_train(
+        &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
+        has_saved ? saved.data_ptr() : nullptr, has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw),
+        ptr(goff), ptr(gm), ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+    return {gin, gw, goff, gm, gb};
+  }
+  // params_ready(grad_weight, grad_bias) runs inside the library call once
+  // both are enqueued; a Python exception is held and re-raised after the
+  // call returns, never thrown through the C ABI
+  struct Ready {
+    const py::function* fn;
+    const at::Tensor* gw;
+    const at::Tensor* gb;
+    std::exception_ptr err;
+  } ready{&*params_ready, &gw, &gb, nullptr};
+  auto tramp = [](void* u) {
+    auto* r = static_cast<Ready*>(u);
+    try {
+      (*r->fn)(r->gw->defined() ? py::cast(*r->gw) : py::none(), r->gb->defined() ? py::cast(*r->gb) : py::none());
+    } catch (...) {
+      r->err = std::current_exception();
+    }
+  };
+  const int rc = dcn_deform_conv2d_backward_overlap(
       &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
       has_saved ? saved.data_ptr() : nullptr, has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw),
-      ptr(goff), ptr(gm), ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+      ptr(goff), ptr(gm), ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input), tramp, &ready);
+  if (ready.err) std::rethrow_exception(ready.err);
+  check_status(rc);
   return {gin, gw, goff, gm, gb};
 }
 
@@ -346,7 +373,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pad_h"), py::arg("pad_w"), py::arg("dilation_h"), py::arg("dilation_w"),
         py::arg("n_weight_grps"), py::arg("n_offset_grps"), py::arg("use_mask"),
         py::arg("output_mask") = std::vector<bool>{true, true, true, true, true},
-        py::arg("saved") = py::none());
+        py::arg("saved") = py::none(), py::arg("params_ready") = py::none());
   m.def("deform_conv2d_forward_train", &deform_conv2d_forward_train,
         "Forward that also returns the device state its backward reuses: (output, saved)");
   m.def("uses_tensor_cores", &uses_tensor_cores, "True when the tcgen05 kernels run this problem");

@@ -44,6 +44,26 @@ def set_training_cache(enabled: bool) -> None:
     _training_cache = bool(enabled)
 
 
+# Called as hook(grad_weight, grad_bias) during each backward, as soon as those
+# two gradients are enqueued on the current stream (either may be None).  On
+# the tensor-core path the input / offset / mask gradients are enqueued after
+# the hook returns, so work the hook starts on another stream -- typically the
+# data-parallel all-reduce of the parameter gradients -- runs alongside them.
+# Work on another stream must wait for an event recorded on the current stream
+# inside the hook, and the caller joins that stream before reading the
+# gradients.  No reference counterpart (its backward returns all gradients at
+# once, mps_deform_conv/__init__.py:245-322).
+_param_grad_hook = None
+
+
+def set_param_grad_hook(hook) -> None:
+    """Install (or clear, with None) the parameter-gradient hook of the backward."""
+    global _param_grad_hook
+    if hook is not None and not callable(hook):
+        raise TypeError("hook must be callable or None")
+    _param_grad_hook = hook
+
+
 def _load_library():
     """Load the native extension; fail loudly when it is missing."""
     try:
@@ -244,7 +264,7 @@ class _DeformConv2dFunction(torch.autograd.Function):
             grad_output, input, weight, offset, mask_t, bias_t,
             stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
             ctx.n_weight_grps, ctx.n_offset_grps, use_mask, output_mask,
-            saved,
+            saved, _param_grad_hook,
         )
         return (grad_input, grad_offset, grad_weight, grad_bias,
                 None, None, None, grad_mask, None, None, None)
@@ -415,4 +435,4 @@ def is_available() -> bool:
 
 
 __all__ = ["deform_conv2d", "DeformConv2d", "ModulatedDeformConv2d", "is_available", "__version__",
-           "set_training_cache"]
+           "set_training_cache", "set_param_grad_hook"]

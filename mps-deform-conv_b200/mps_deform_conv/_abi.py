@@ -38,6 +38,8 @@ class DcnConvDesc(ctypes.Structure):
 
 # name -> (restype, argtypes); the exported surface of include/dcn_b200.h
 _D = ctypes.POINTER(DcnConvDesc)
+# void (*dcn_params_ready_fn)(void* user_data)
+PARAMS_READY_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 _V = ctypes.c_void_p
 _SZ = ctypes.c_size_t
 SIGNATURES = {
@@ -62,6 +64,8 @@ SIGNATURES = {
     "dcn_deform_conv2d_forward_train": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
     "dcn_deform_conv2d_backward_train": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V,
                                                         _V, _SZ, _V]),
+    "dcn_deform_conv2d_backward_overlap": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V,
+                                                          _V, _SZ, _V, PARAMS_READY_FN, _V]),
     "dcn_device_status": (ctypes.c_int, [_V]),
     "dcn_uses_tensor_cores": (ctypes.c_int, [_D]),
 }

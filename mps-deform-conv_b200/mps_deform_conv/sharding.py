@@ -10,6 +10,9 @@ holds the two host-side pieces of that scheme:
   packed into a single flat bucket, so a step issues one collective instead of
   one per tensor.  Works on any torch.distributed backend (NCCL over NVLink on
   GPUs, gloo on CPU).
+* ``OverlappedParamAllReduce`` -- the same all-reduce started from the
+  backward's parameter-gradient hook (``set_param_grad_hook``) on a side
+  stream, so it runs while the input / offset / mask gradients are computed.
 """
 from __future__ import annotations
 
@@ -50,3 +53,43 @@ def allreduce_param_grads(grads: Sequence[Optional[torch.Tensor]], group=None,
         g.copy_(flat[off:off + n].view_as(g))
         off += n
     return list(grads)
+
+
+class OverlappedParamAllReduce:
+    """Parameter-gradient hook that all-reduces grad_weight / grad_bias on a
+    side stream while the rest of the backward runs.
+
+    Install with ``mps_deform_conv.set_param_grad_hook(h)``; after the backward
+    returns, call ``h.wait()`` before reading the parameter gradients (it makes
+    the current stream wait for the side stream; on CPU the reduction already
+    ran inside the hook).  The gradients are reduced in place, so the caller
+    keeps them alive until ``wait()``.  Every rank must run the same layers in
+    the same order, as for any collective.
+    """
+
+    def __init__(self, group=None, average: bool = False, stream=None):
+        self.group = group
+        self.average = average
+        self._stream = stream
+        self.calls = 0
+
+    def _side_stream(self):
+        if self._stream is None:
+            self._stream = torch.cuda.Stream()
+        return self._stream
+
+    def __call__(self, grad_weight, grad_bias):
+        self.calls += 1
+        grads = [grad_weight, grad_bias]
+        dev = next((g.device for g in grads if g is not None), None)
+        if dev is None or dev.type != "cuda":
+            allreduce_param_grads(grads, self.group, self.average)
+            return
+        side = self._side_stream()
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            allreduce_param_grads(grads, self.group, self.average)
+
+    def wait(self) -> None:
+        if self._stream is not None:
+            torch.cuda.current_stream().wait_stream(self._stream)

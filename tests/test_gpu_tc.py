@@ -186,6 +186,33 @@ def test_tc_autograd_training_cache(name, cache, cuda):
         assert rel_err(to_np(leaves["mask"].grad), rgm) <= tol
 
 
+@pytest.mark.parametrize("cache", [True, False])
+def test_tc_weight_grad_deterministic(cache, cuda):
+    """grad_weight: each split of the pixel range stores its partial sum and
+    the splits are added in a fixed order, so repeated backward passes are
+    bitwise equal, with the saved column tiles and with the gathering wgrad."""
+    import mps_deform_conv as mdc
+    lib = mdc._get_lib()
+    T = _make(SHAPES["c128_g2_og4_dil2"], torch.bfloat16, cuda, seed=17)
+    T["input"] = T["input"].repeat(16, 1, 1, 1)  # 32 x 100 pixels: several pixel splits
+    T["offset"] = T["offset"].repeat(16, 1, 1, 1)
+    T["mask"] = T["mask"].repeat(16, 1, 1, 1)
+    T["grad_output"] = T["grad_output"].repeat(16, 1, 1, 1)
+    st, pd, dl = T["stride"], T["padding"], T["dilation"]
+    args = (T["input"], T["weight"], T["offset"], T["mask"], T["bias"], st[0], st[1], pd[0], pd[1], dl[0], dl[1],
+            2, 4, True)
+    saved = lib.deform_conv2d_forward_train(*args)[1] if cache else None
+    sel = [False, True, False, False, False]
+    gw = [lib.deform_conv2d_backward(T["grad_output"], *args, sel, saved)[1] for _ in range(3)]
+    torch.cuda.synchronize()
+    lib.device_status()
+    assert torch.equal(gw[0], gw[1]) and torch.equal(gw[0], gw[2])
+    _, _, rgw, _, _ = oracle.backward(T["grad_output"][:2], T["input"][:2], T["offset"][:2], T["weight"], st, pd,
+                                      dl, T["mask"][:2], False)
+    assert torch.isfinite(gw[0]).all()
+    assert rel_err(to_np(gw[0]) / 16.0, rgw) <= TOL["bfloat16"]
+
+
 def test_abi_training_pair_matches_plain_calls(cuda):
     """dcn_deform_conv2d_forward_train / _backward_train through ctypes give the
     same results as the plain forward / backward."""

@@ -12,7 +12,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from mps_deform_conv.sharding import allreduce_param_grads, shard_range
+from mps_deform_conv.sharding import OverlappedParamAllReduce, allreduce_param_grads, shard_range
 
 
 def test_shard_range_partitions():
@@ -58,7 +58,7 @@ def _param_grads(x, w, b, off, m, go):
     return w.grad, b.grad
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="serial"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -67,17 +67,24 @@ def _worker(rank, world, port, q):
         x, w, b, off, m, go = _problem()
         s, c = shard_range(x.shape[0], world, rank)
         gw, gb = _param_grads(x[s:s + c], w, b, off[s:s + c], m[s:s + c], go[s:s + c])
-        allreduce_param_grads([gw, None, gb])
+        if mode == "hook":  # the backward's parameter-gradient hook, CPU tensors
+            hook = OverlappedParamAllReduce()
+            hook(gw, gb)
+            hook.wait()
+            assert hook.calls == 1
+        else:
+            allreduce_param_grads([gw, None, gb])
         q.put((rank, gw.numpy().copy(), gb.numpy().copy()))  # by value: the sender exits
     finally:
         dist.destroy_process_group()
 
 
-def test_two_rank_gloo_allreduce_matches_full_batch():
+@pytest.mark.parametrize("mode", ["serial", "hook"])
+def test_two_rank_gloo_allreduce_matches_full_batch(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(2)]
