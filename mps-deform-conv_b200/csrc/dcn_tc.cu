@@ -130,16 +130,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
     // ------------------------------------------------ producers
     const int r = warp * 8 + (lane >> 2), cq = lane & 3;
     const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
+    uint8_t* cols_tile = a.cols ? static_cast<uint8_t*>(a.cols) +
+                                      ((size_t)grp * gridDim.x + tile) * a.nkc * (size_t)A_STAGE_BYTES
+                                : nullptr;
+    Ring ring{0, S, 0u};
     const bool ok = gather_run<T>(
-        g, xh, off, msk, pc, r, cq, grp * g.Cig, 0, a.nkc, abort_flag, a.status, ST_PROD,
-        [&](int i, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& par, uint32_t& fb) {
-          const int s = i % S;
+        g, xh, off, msk, pc, r, cq, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
+        [&](int i, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
           t = smem + L.a + s * A_STAGE_BYTES;
-          gt = a.cols ? static_cast<uint8_t*>(a.cols) +
-                            (((size_t)grp * gridDim.x + tile) * a.nkc + i) * (size_t)A_STAGE_BYTES
-                      : nullptr;
+          gt = cols_tile ? cols_tile + (size_t)i * A_STAGE_BYTES : nullptr;
           eb = empty(s);
-          par = ((i / S) & 1) ^ 1;
           fb = a_full(s);
         });
     // ------------------------------------------------ epilogue
@@ -256,15 +256,17 @@ __global__ void nchw_to_nhwc_kernel(const T* __restrict__ x, T* __restrict__ xh,
   }
 }
 
-// weight [Co][Cig][T] -> [G][NKC][Cog][64], K chunk kc = (cc, t) with t
-// fastest, rows 128-byte swizzled (chunk q of row co at q ^ (co % 8)).
+// weight [Co][Cig][T] -> [G][NKC][Cog][64] in the producers' gather order,
+// K chunk kc = t * (Cig/64) + cc (channel chunk fastest), rows 128-byte
+// swizzled (chunk q of row co at q ^ (co % 8)).
 // blockIdx.x = grp * nkc + kc; a thread gathers the 8 channels of one 16-byte
 // chunk and stores it whole.
 template <typename T>
 __global__ void weight_swizzle_kernel(const T* __restrict__ w, T* __restrict__ wsw, int Cog, int Cig,
                                       int T_, int nkc) {
   const int grp = blockIdx.x / nkc, kc = blockIdx.x - grp * nkc;
-  const int t = kc % T_, cc = kc / T_;
+  const int ncc = Cig / BK;
+  const int t = kc / ncc, cc = kc - t * ncc;
   const int i = blockIdx.y * blockDim.x + threadIdx.x;  // (co, chunk q)
   if (i >= Cog * 8) return;
   const int co = i >> 3, q = i & 7;
@@ -299,6 +301,8 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   if (g.cpo % 8 != 0) return false;                  // 16-byte vectors inside one offset group
   if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N per MMA: Cog or Cog/2, multiple of 16
   if (pick_stages(g.Cog) < 2) return false;
+  // the gather addresses one image's input and offset planes with 32-bit offsets
+  if ((long long)g.H * g.W * g.C >= (1LL << 31) || (long long)g.OG * 2 * g.T * g.HWo >= (1LL << 31)) return false;
   return true;
 }
 

@@ -46,10 +46,10 @@ struct WgradArgs {
   const void* xh;
   const void* off;
   const void* msk;
-  float* gwp;      // per-split partial gW [splits][Co][nkc][64] fp32 (kc = cc*T + t)
+  float* gwp;      // per-split partial gW [splits][Co][nkc][64] fp32 (kc in gather order)
   int* status;
   Geom g;
-  int nkc;         // K chunks per group, kc = cc*T + t
+  int nkc;         // K chunks per group, kc = t * (Cig/64) + cc (gather order)
   int nkg;         // K chunks per CTA
   int mh;          // M halves of 128 output channels
   int ncb;         // 64-channel blocks of grad_output loaded per tile
@@ -138,16 +138,14 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
     // -------------------------------------------- col-tile producers
     const int r = warp * 8 + (lane >> 2), cq = lane & 3;
     bool ok = true;
+    Ring ring{0, BS, 0u};  // continues across the CTA's pixel tiles
     for (int li = 0; li < nt && ok; ++li) {
       const PixelCtx pc = pixel_ctx(g, (long long)(t0 + li) * BM + r);
-      ok = gather_run<T>(g, xh, off, msk, pc, r, cq, grp * g.Cig, k0, nk, abort_flag, a.status, ST_W_PROD,
-                         [&](int i, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& par, uint32_t& fb) {
-                           const int j = li * nk + i;
-                           const int s = j % BS;
+      ok = gather_run<T>(g, xh, off, msk, pc, r, cq, grp * g.Cig, k0, nk, ring, abort_flag, a.status, ST_W_PROD,
+                         [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
                            t = smem + L.b + s * A_STAGE_BYTES;
                            gt = nullptr;
                            eb = b_empty(s);
-                           par = ((j / BS) & 1) ^ 1;
                            fb = b_full(s);
                          });
     }
@@ -853,12 +851,12 @@ __global__ void convert_multi_kernel(const ConvertJobs jobs) {
 }
 
 // gW [Co][Cig][T] = sum over splits (in split order) of the partials
-// [splits][Co][nkc][64], and gB = gb32 in T when gb is given.  One CTA per
-// (output channel, 64-channel block cc):
-// the 64*T partials of one split are one contiguous run [t][j] (kc = cc*T + t),
-// read as float4 and summed in registers; a padded shared-memory tile turns
-// them into the contiguous output run [j][t].  Dynamic shared memory:
-// T * 65 floats.
+// [splits][Co][nkc][64] (kc in the producers' gather order t * (Cig/64) + cc),
+// and gB = gb32 in T when gb is given.  One CTA per (output channel,
+// 64-channel block cc): the 64 partials of each tap are contiguous, read as
+// float4 and summed over the splits in registers; a padded shared-memory tile
+// [t][j] turns them into the contiguous output run [j][t].  Dynamic shared
+// memory: T * 65 floats.
 constexpr int WR_THREADS = 128;
 inline size_t wgrad_reduce_smem(int T_) { return sizeof(float) * (size_t)T_ * 65; }
 
@@ -873,11 +871,12 @@ wgrad_reduce_kernel(const float* __restrict__ gwp, T* __restrict__ gw, const flo
   const int co = blockIdx.x / ncc, cc = blockIdx.x - co * ncc;
   const int nkc = ncc * T_;
   const size_t split_stride4 = (size_t)Co * nkc * 16;
-  const float4* src = reinterpret_cast<const float4*>(gwp + ((size_t)co * nkc + (size_t)cc * T_) * 64);
+  const float4* src = reinterpret_cast<const float4*>(gwp + ((size_t)co * nkc + cc) * 64);
   for (int i = threadIdx.x; i < 16 * T_; i += WR_THREADS) {
-    float4 acc = src[i];
+    const size_t at = (size_t)(i >> 4) * ncc * 16 + (i & 15);  // tap i/16, float4 i%16
+    float4 acc = src[at];
     for (int sp = 1; sp < splits; ++sp) {
-      const float4 v = src[sp * split_stride4 + i];
+      const float4 v = src[sp * split_stride4 + at];
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     float* row = wr_tile + (i >> 4) * 65 + (i & 15) * 4;

@@ -169,58 +169,162 @@ struct KWalk {
   }
 };
 
-// One producer thread's share of a run of K chunks for one pixel tile: per
-// chunk it waits for its stage to be free, gathers 2 x 16 bytes of 4 corners,
-// blends, and writes its two 16-byte chunks of row r into the swizzled tile.
-// `stage_of(i)` returns (shared-memory tile base, global tile copy or null,
-// empty-barrier, parity, full-barrier) for the i-th chunk of the run; returns
-// false if a wait expired.
+// Gather order of the producers' K chunks: kc = t * ncc + cc (ncc = Cig / 64
+// channel chunks per tap), channel chunk fastest, so that consecutive chunks
+// of one tap whose channels lie in the same offset group share the sampling
+// point.  The forward's A/B operand tiles, its saved column tiles and the
+// weight-gradient partials all follow this order (dgrad uses its own, KWalk).
+struct GatherWalk {
+  int t, cc, ti, tj;
+  __device__ __forceinline__ void start(const Geom& g, int kc, int ncc) {
+    t = kc / ncc;
+    cc = kc - t * ncc;
+    ti = t / g.kw;
+    tj = t - ti * g.kw;
+  }
+  __device__ __forceinline__ void next(const Geom& g, int ncc) {
+    if (++cc == ncc) {
+      cc = 0;
+      ++t;
+      if (++tj == g.kw) { tj = 0; ++ti; }
+    }
+  }
+};
+
+// Offset group of a lane's 8-channel vector, tracked as the channel chunk
+// advances by 64 channels (no division per chunk): og = c / cpo, rem = c % cpo.
+struct OgTrack {
+  int og, rem;
+  __device__ __forceinline__ void set(int c, int cpo) {
+    og = c / cpo;
+    rem = c - og * cpo;
+  }
+  __device__ __forceinline__ void step64(int cpo) {
+    rem += BK;
+    while (rem >= cpo) { rem -= cpo; ++og; }
+  }
+};
+
+// Ring position of a pipeline of S stages: stage s and the phase bit of its
+// barriers (flips each time the ring wraps).
+struct Ring {
+  int s, S;
+  uint32_t ph;
+  __device__ __forceinline__ void next() {
+    if (++s == S) { s = 0; ph ^= 1u; }
+  }
+};
+
+// Corners of one sample as 32-bit element offsets of channel 0 within the
+// image's channels-last plane (H*W*C < 2^31) and weights including the mask.
+struct CornerSet32 {
+  int off[4];
+  float w[4];
+};
+
+template <typename T>
+__device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCtx& pc, const RawSample<T>& r,
+                                                    int ti, int tj) {
+  CornerSet32 cs;
+  const SamplePos sp = sample_pos(pc.y0 + ti * g.dh, pc.x0 + tj * g.dw, to_f(r.dy), to_f(r.dx));
+  const Corners c = corners_of(sp, g.H, g.W);
+  const float m = pc.valid ? to_f(r.m) : 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    cs.w[k] = c.w[k] * m;
+    cs.off[k] = c.idx[k] * g.C;
+  }
+  return cs;
+}
+
+// One producer thread's share of a run of K chunks for one pixel tile (gather
+// order above): per chunk it waits for its stage to be free, gathers 2 x 16
+// bytes of 4 corners, blends, and writes its two 16-byte chunks of row r into
+// the swizzled tile.  The sampling point and the offset / mask loads are
+// reused while consecutive chunks share the tap and the offset groups.
+// `ring` is the stage ring position (advanced once per chunk);
+// `stage_of(i, s, tile, gtile, empty_bar, full_bar)` gives the shared-memory
+// tile of stage s, the global copy of the i-th tile of the run (or null) and
+// the barriers.  Returns false if a wait expired.  Per image the offset plane
+// (OG*2*T*Ho*Wo elements) and the input plane (H*W*C) are below 2^31.
 template <typename T, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
                                            const PixelCtx& pc, int r, int cq, int cbase_grp, int kc0,
-                                           int nk, volatile int* abort_flag, int* status, int code,
-                                           StageFn&& stage_of) {
-  KWalk kw;
-  kw.start(g, kc0);
-  int og0 = (cbase_grp + kw.cc * BK + cq * 8) / g.cpo;
-  int og1 = (cbase_grp + kw.cc * BK + cq * 8 + 32) / g.cpo;
-  RawSample<T> raw0 = load_raw(g, off, msk, pc, og0, kw.t);
-  RawSample<T> raw1 = (og1 == og0) ? raw0 : load_raw(g, off, msk, pc, og1, kw.t);
+                                           int nk, Ring& ring, volatile int* abort_flag, int* status,
+                                           int code, StageFn&& stage_of) {
+  const int ncc = g.Cig / BK;
+  const T* __restrict__ ximg = xh + (size_t)pc.img * g.C;
+  const T* __restrict__ offp = off + (size_t)pc.b * g.OG * 2 * g.T * g.HWo + pc.p;
+  const T* __restrict__ mskp = msk ? msk + (size_t)pc.b * g.OG * g.T * g.HWo + pc.p : nullptr;
+  auto load = [&](int o, int t) {
+    RawSample<T> rs;
+    const int ob = (o * 2 * g.T + 2 * t) * g.HWo;
+    rs.dy = offp[ob];
+    rs.dx = offp[ob + g.HWo];
+    rs.m = mskp ? mskp[(o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    return rs;
+  };
+  GatherWalk kw;
+  kw.start(g, kc0, ncc);
+  // offset groups of the lane's two vectors (channels cq*8 and cq*8 + 32 of
+  // the chunk) at chunk cc = 0 and at the current chunk
+  OgTrack a0, b0, a, b;
+  a0.set(cbase_grp + cq * 8, g.cpo);
+  b0.set(cbase_grp + cq * 8 + 32, g.cpo);
+  a.set(cbase_grp + kw.cc * BK + cq * 8, g.cpo);
+  b.set(cbase_grp + kw.cc * BK + cq * 8 + 32, g.cpo);
+  RawSample<T> raw0 = load(a.og, kw.t);
+  RawSample<T> raw1 = (b.og == a.og) ? raw0 : load(b.og, kw.t);
+  CornerSet32 cs0, cs1;
+  bool reuse = false;  // cs0 / cs1 already hold this chunk's corners
   for (int i = 0; i < nk; ++i) {
-    const CornerSet cs0 = corner_set(g, pc, raw0, kw.ti, kw.tj);
-    const CornerSet cs1 = (og1 == og0) ? cs0 : corner_set(g, pc, raw1, kw.ti, kw.tj);
+    if (!reuse) {
+      cs0 = corner_set32(g, pc, raw0, kw.ti, kw.tj);
+      cs1 = (b.og == a.og) ? cs0 : corner_set32(g, pc, raw1, kw.ti, kw.tj);
+    }
     const int c0 = cbase_grp + kw.cc * BK + cq * 8;
     uint4 v0[4], v1[4];
-    load_corners(xh, cs0, c0, v0);
-    load_corners(xh, cs1, c0 + 32, v1);
-    // prefetch the next chunk's offsets and mask
-    KWalk nx = kw;
-    nx.next(g);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v0[k] = (cs0.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(ximg + cs0.off[k] + c0))
+                                : make_uint4(0, 0, 0, 0);
+      v1[k] = (cs1.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(ximg + cs1.off[k] + c0 + 32))
+                                : make_uint4(0, 0, 0, 0);
+    }
+    // the next chunk: same sampling point, or prefetch its offsets and mask
     if (i + 1 < nk) {
-      if (nx.cc != kw.cc) {
-        og0 = (cbase_grp + nx.cc * BK + cq * 8) / g.cpo;
-        og1 = (cbase_grp + nx.cc * BK + cq * 8 + 32) / g.cpo;
+      const int pt = kw.t, pa = a.og, pb = b.og;
+      kw.next(g, ncc);
+      if (kw.cc == 0) {
+        a = a0;
+        b = b0;
+      } else {
+        a.step64(g.cpo);
+        b.step64(g.cpo);
       }
-      raw0 = load_raw(g, off, msk, pc, og0, nx.t);
-      if (og1 != og0) raw1 = load_raw(g, off, msk, pc, og1, nx.t);
+      reuse = kw.t == pt && a.og == pa && b.og == pb;
+      if (!reuse) {
+        raw0 = load(a.og, kw.t);
+        if (b.og != a.og) raw1 = load(b.og, kw.t);
+      }
     }
     uint8_t* tile;
     uint8_t* gtile;  // global copy of the tile image, or null
-    uint32_t empty_bar, parity, full_bar;
-    stage_of(i, tile, gtile, empty_bar, parity, full_bar);
-    const uint4 b0 = blend8<T>(v0, cs0.w), b1 = blend8<T>(v1, cs1.w);
+    uint32_t empty_bar, full_bar;
+    stage_of(i, ring.s, tile, gtile, empty_bar, full_bar);
+    const uint4 o0v = blend8<T>(v0, cs0.w), o1v = blend8<T>(v1, cs1.w);
     const int o0 = r * 128 + ((cq ^ (r & 7)) << 4), o1 = r * 128 + (((cq + 4) ^ (r & 7)) << 4);
     if (gtile) {  // streaming stores: keep L2 for the gather
-      __stcs(reinterpret_cast<uint4*>(gtile + o0), b0);
-      __stcs(reinterpret_cast<uint4*>(gtile + o1), b1);
+      __stcs(reinterpret_cast<uint4*>(gtile + o0), o0v);
+      __stcs(reinterpret_cast<uint4*>(gtile + o1), o1v);
     }
-    if (!mbar_wait(empty_bar, parity, abort_flag, status, code)) return false;
-    *reinterpret_cast<uint4*>(tile + o0) = b0;
-    *reinterpret_cast<uint4*>(tile + o1) = b1;
+    if (!mbar_wait(empty_bar, ring.ph ^ 1u, abort_flag, status, code)) return false;
+    *reinterpret_cast<uint4*>(tile + o0) = o0v;
+    *reinterpret_cast<uint4*>(tile + o1) = o1v;
     fence_async_shared();
     mbar_arrive(full_bar);
-    kw = nx;
+    ring.next();
   }
   return true;
 }
