@@ -431,19 +431,30 @@ struct DgWarpSmem {
 // 16-byte stores (8 rows per phase) and for the 4-lanes-per-row loads.
 __device__ __forceinline__ int slab_pos(int r, int k) { return (k ^ ((r >> 1) & 3)) * 4; }
 
+// Per-warp epilogue scratch of the 32-channel-slab variant (offset groups of
+// a multiple of 32 channels, so a slab has one sample per pixel): the slab of
+// 32 rows x 32 channels (16-byte chunk k of row r at chunk k ^ (r & 7), so
+// that 8 rows' stores and 8 lanes' loads of one row both hit distinct banks)
+// and one sample per row (corner pixel indices, bilinear weights, fy, fx,
+// mask, valid bits; 48-byte rows: 4 rows read together hit distinct banks).
+struct DgWarpSmem32 {
+  float slab[32][32];
+  uint32_t tab[32][12];
+};
+
 // Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
 // streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each;
 // then the epilogue warps' scratch.
 struct DgradSmem {
   uint32_t a, b, b_stage, epi, bar, total;
 };
-__host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages) {
+__host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages, int sw) {
   DgradSmem L;
   L.a = 0;
   L.b = (uint32_t)kb * A_STAGE_BYTES;
   L.b_stage = 8192u;
   L.epi = L.b + b_stages * L.b_stage;
-  L.bar = L.epi + D_EPI_WARPS * (uint32_t)sizeof(DgWarpSmem);
+  L.bar = L.epi + D_EPI_WARPS * (uint32_t)(sw == 32 ? sizeof(DgWarpSmem32) : sizeof(DgWarpSmem));
   L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
   return L;
 }
@@ -453,14 +464,18 @@ __device__ __forceinline__ void red_v4(float* p, float a, float b, float c, floa
                : "memory");
 }
 
-template <typename T>
+// SW = channels per epilogue slab: 32 when the offset groups are a multiple
+// of 32 channels (8 lanes x 4 channels per pixel: each corner's 32 fp32
+// gradients are one 128-byte line, half the lines per byte of SW = 16), else
+// 16 (4 lanes x 4 channels, up to 2 offset groups per slab).
+template <typename T, int SW>
 __global__ void __launch_bounds__(D_NTHREADS, 1)
 dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Geom& g = a.g;
   const int S = a.b_stages;
-  const DgradSmem L = dgrad_smem(a.kb, S);
+  const DgradSmem L = dgrad_smem(a.kb, S, SW);
   const uint32_t sbase = smem_addr(smem);
   const uint32_t bar0 = sbase + L.bar;
   const uint32_t a_full = bar0;
@@ -496,7 +511,162 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < D_EPI_WARPS) {
+  if (warp < D_EPI_WARPS && SW == 32) {
+    // -------------------------------------------- epilogue, 32-channel slabs
+    // Per slab of a gcol tile (one offset group):
+    //  (1) row owner (lane = TMEM row = pixel): reads its 32 gcol values from
+    //      TMEM into the warp's slab and, when the offset group changes,
+    //      computes the sample's corners into its table row;
+    //  (2) 8 lanes per pixel, 4 channels per lane, 4 pixels per instruction:
+    //      corner loads and red.global.add.v4.f32 scatters cover whole lines;
+    //      the offset/mask partial sums are reduced over the pixel's 8 lanes
+    //      by shuffles and taken by the row owner, which adds them to global
+    //      memory once per (pixel, offset group, K chunk).
+    const T* xh = static_cast<const T*>(a.xh);
+    const T* off = static_cast<const T*>(a.off);
+    const T* msk = static_cast<const T*>(a.msk);
+    const int e = warp >> 2, q = warp & 3;
+    DgWarpSmem32* ws = reinterpret_cast<DgWarpSmem32*>(smem + L.epi) + warp;
+    const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
+    const int j8 = lane & 7, rsub = lane >> 3;
+    bool ok = true;
+    for (int i = e; i < nkc_cta; i += D_NBUF) {
+      const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
+      ok = __all_sync(0xffffffffu, ready);
+      if (!ok) break;
+      tc_fence_after();
+      KWalk kw;
+      kw.start(g, kc_lo + i);
+      const int cbase = grp * g.Cig + kw.cc * BK;
+      int tab_o = -1, acc_o = -1;
+      float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
+      auto flush = [&]() {
+        if (acc_o >= 0 && pc.valid) {
+          const long long ob = ((long long)(pc.b * g.OG + acc_o) * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          atomicAdd(a.goff32 + ob, run_gy);
+          atomicAdd(a.goff32 + ob + g.HWo, run_gx);
+          if (g.use_mask)
+            atomicAdd(a.gmsk32 + ((long long)(pc.b * g.OG + acc_o) * g.T + kw.t) * g.HWo + pc.p, run_gm);
+        }
+        run_gy = run_gx = run_gm = 0.f;
+      };
+#pragma unroll 1
+      for (int sl = 0; sl < 2; ++sl) {
+        // ---- phase 1: row owner
+        {
+          uint32_t acc0[16], acc1[16];
+          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64 + sl * 32);
+          tmem_ld16(taddr, acc0);
+          tmem_ld16(taddr + 16, acc1);
+          tmem_ld_wait();
+          if (sl == 1) {  // last read of this TMEM buffer: let the MMA reuse it
+            tc_fence_before();
+            mbar_arrive(d_empty(e));
+          }
+          float* srow = ws->slab[lane];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            *reinterpret_cast<uint4*>(srow + ((k ^ (lane & 7)) << 2)) =
+                make_uint4(acc0[4 * k], acc0[4 * k + 1], acc0[4 * k + 2], acc0[4 * k + 3]);
+            *reinterpret_cast<uint4*>(srow + (((k + 4) ^ (lane & 7)) << 2)) =
+                make_uint4(acc1[4 * k], acc1[4 * k + 1], acc1[4 * k + 2], acc1[4 * k + 3]);
+          }
+        }
+        const int o = (cbase + sl * 32) / g.cpo;  // warp-uniform
+        if (o != tab_o) {
+          tab_o = o;
+          const RawSample<T> raw = load_raw(g, off, msk, pc, o, kw.t);
+          const SamplePos sp = sample_pos(pc.y0 + kw.ti * g.dh, pc.x0 + kw.tj * g.dw, to_f(raw.dy), to_f(raw.dx));
+          const Corners cs = corners_of(sp, g.H, g.W);
+          const CoordCorners c4 = coord_corners_of(sp, g.H, g.W);
+          uint32_t cvb = 0;
+          int cidx[4];
+          float cw[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const bool v = pc.valid && c4.v[k];
+            cvb |= (v ? 1u : 0u) << k;
+            cidx[k] = v ? (int)(pc.img + c4.idx[k]) : 0;
+            cw[k] = pc.valid ? cs.w[k] : 0.f;
+          }
+          uint32_t* trow = ws->tab[lane];
+          *reinterpret_cast<uint4*>(trow) = make_uint4(cidx[0], cidx[1], cidx[2], cidx[3]);
+          *reinterpret_cast<uint4*>(trow + 4) = make_uint4(__float_as_uint(cw[0]), __float_as_uint(cw[1]),
+                                                           __float_as_uint(cw[2]), __float_as_uint(cw[3]));
+          *reinterpret_cast<uint4*>(trow + 8) =
+              make_uint4(__float_as_uint(c4.fy), __float_as_uint(c4.fx),
+                         __float_as_uint(pc.valid ? to_f(raw.m) : 0.f), cvb);
+        }
+        if (o != acc_o) {
+          flush();
+          acc_o = o;
+        }
+        __syncwarp();
+        // ---- phase 2: 8 lanes per pixel, 4 pixels per step
+        const int cslab = cbase + sl * 32 + j8 * 4;
+#pragma unroll 1
+        for (int it = 0; it < 8; ++it) {
+          const int rr = it * 4 + rsub;
+          const uint32_t* tr = ws->tab[rr];
+          const uint4 tb = *reinterpret_cast<const uint4*>(tr);
+          const uint4 tw = *reinterpret_cast<const uint4*>(tr + 4);
+          const uint4 tx = *reinterpret_cast<const uint4*>(tr + 8);
+          const float4 gv = *reinterpret_cast<const float4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2));
+          const int ci[4] = {(int)tb.x, (int)tb.y, (int)tb.z, (int)tb.w};
+          const float w[4] = {__uint_as_float(tw.x), __uint_as_float(tw.y), __uint_as_float(tw.z),
+                              __uint_as_float(tw.w)};
+          const float fy = __uint_as_float(tx.x), fx = __uint_as_float(tx.y), m = __uint_as_float(tx.z);
+          const uint32_t cv = tx.w;
+          uint2 xv[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + (long long)ci[k] * g.C + cslab))
+                                   : make_uint2(0, 0);
+          const float gvv[4] = {gv.x, gv.y, gv.z, gv.w};
+          float pgy = 0.f, pgx = 0.f, pgm = 0.f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float2 f0 = Vec<T>::unpack((&xv[0].x)[h]), f1 = Vec<T>::unpack((&xv[1].x)[h]);
+            const float2 f2 = Vec<T>::unpack((&xv[2].x)[h]), f3 = Vec<T>::unpack((&xv[3].x)[h]);
+            const float ga = gvv[2 * h], gb = gvv[2 * h + 1];
+            pgm += ga * (w[0] * f0.x + w[1] * f1.x + w[2] * f2.x + w[3] * f3.x);
+            pgm += gb * (w[0] * f0.y + w[1] * f1.y + w[2] * f2.y + w[3] * f3.y);
+            pgy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
+            pgy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
+            pgx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
+            pgx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float wk = w[k] * m;
+            if (wk != 0.f)
+              red_v4(a.gi32 + (long long)ci[k] * g.C + cslab, wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
+          }
+          pgy *= m;
+          pgx *= m;
+#pragma unroll
+          for (int sh = 1; sh < 8; sh <<= 1) {
+            pgy += __shfl_xor_sync(0xffffffffu, pgy, sh);
+            pgx += __shfl_xor_sync(0xffffffffu, pgx, sh);
+            pgm += __shfl_xor_sync(0xffffffffu, pgm, sh);
+          }
+          // rows it*4 .. it*4+3 are owned by lanes it*4 .. it*4+3; their sums
+          // sit in lanes 0, 8, 16, 24
+          const int src = (lane & 3) * 8;
+          const float sy = __shfl_sync(0xffffffffu, pgy, src);
+          const float sx = __shfl_sync(0xffffffffu, pgx, src);
+          const float sm = __shfl_sync(0xffffffffu, pgm, src);
+          if ((lane >> 2) == it) {
+            run_gy += sy;
+            run_gx += sx;
+            run_gm += sm;
+          }
+        }
+        __syncwarp();
+      }
+      flush();
+    }
+  } else if (warp < D_EPI_WARPS) {
     // -------------------------------------------- epilogue: col2im + col2im_coord
     // Two phases per 16-channel slab of a gcol tile:
     //  (1) row owner (lane = TMEM row = pixel): reads its 16 gcol values from
@@ -1074,11 +1244,13 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
     a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
     a.b_stages = 4;
-    while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) --a.b_stages;
-    if (dgrad_smem(KB, a.b_stages).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
+    const int sw = g.cpo % 32 == 0 ? 32 : 16;  // epilogue slab width (see the kernel)
+    while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) --a.b_stages;
+    if (dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
     a.idesc = idesc_f16(BM, 64, bf16);
-    const int smem = (int)dgrad_smem(KB, a.b_stages).total + 1024;
-    if ((e = cudaFuncSetAttribute(dcn_dgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+    const int smem = (int)dgrad_smem(KB, a.b_stages, sw).total + 1024;
+    auto kern = sw == 32 ? dcn_dgrad_tc_kernel<T, 32> : dcn_dgrad_tc_kernel<T, 16>;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
       return e;
     // split the K chunks of a tile over ksplit CTAs when that fills the last
     // wave of 148 SMs (one CTA per SM) better; keep >= 4 chunks per CTA
@@ -1090,7 +1262,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       if (eff > best + 0.05) { best = eff; ksplit = k; }
     }
     KernelScope ks("dcn_dgrad_tc", st);
-    dcn_dgrad_tc_kernel<T><<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
+    kern<<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   // ---- finalize
