@@ -465,9 +465,10 @@ __device__ __forceinline__ void red_v4(float* p, float a, float b, float c, floa
 }
 
 // SW = channels per epilogue slab: 32 when the offset groups are a multiple
-// of 32 channels (8 lanes x 4 channels per pixel: each corner's 32 fp32
-// gradients are one 128-byte line, half the lines per byte of SW = 16), else
-// 16 (4 lanes x 4 channels, up to 2 offset groups per slab).
+// of 32 channels and B*H*W*C < 2^31 (8 lanes x 4 channels per pixel: each
+// corner's 32 fp32 gradients are one 128-byte line, half the lines per byte
+// of SW = 16; 32-bit element offsets), else 16 (4 lanes x 4 channels, up to
+// 2 offset groups per slab).
 template <typename T, int SW>
 __global__ void __launch_bounds__(D_NTHREADS, 1)
 dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
@@ -586,7 +587,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           for (int k = 0; k < 4; ++k) {
             const bool v = pc.valid && c4.v[k];
             cvb |= (v ? 1u : 0u) << k;
-            cidx[k] = v ? (int)(pc.img + c4.idx[k]) : 0;
+            cidx[k] = v ? (int)((pc.img + c4.idx[k]) * g.C) : 0;  // element offset, B*H*W*C < 2^31
             cw[k] = pc.valid ? cs.w[k] : 0.f;
           }
           uint32_t* trow = ws->tab[lane];
@@ -612,7 +613,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           const uint4 tw = *reinterpret_cast<const uint4*>(tr + 4);
           const uint4 tx = *reinterpret_cast<const uint4*>(tr + 8);
           const float4 gv = *reinterpret_cast<const float4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2));
-          const int ci[4] = {(int)tb.x, (int)tb.y, (int)tb.z, (int)tb.w};
+          const uint32_t eo[4] = {tb.x + (uint32_t)cslab, tb.y + (uint32_t)cslab, tb.z + (uint32_t)cslab,
+                                  tb.w + (uint32_t)cslab};
           const float w[4] = {__uint_as_float(tw.x), __uint_as_float(tw.y), __uint_as_float(tw.z),
                               __uint_as_float(tw.w)};
           const float fy = __uint_as_float(tx.x), fx = __uint_as_float(tx.y), m = __uint_as_float(tx.z);
@@ -620,30 +622,23 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           uint2 xv[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + (long long)ci[k] * g.C + cslab))
-                                   : make_uint2(0, 0);
-          const float gvv[4] = {gv.x, gv.y, gv.z, gv.w};
-          float pgy = 0.f, pgx = 0.f, pgm = 0.f;
+            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + eo[k])) : make_uint2(0, 0);
+          // d[k] = sum over the lane's 4 channels of gcol * x at corner k; the
+          // mask, offset-y and offset-x partial sums are linear in them
+          float d[4];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float2 f0 = Vec<T>::unpack((&xv[0].x)[h]), f1 = Vec<T>::unpack((&xv[1].x)[h]);
-            const float2 f2 = Vec<T>::unpack((&xv[2].x)[h]), f3 = Vec<T>::unpack((&xv[3].x)[h]);
-            const float ga = gvv[2 * h], gb = gvv[2 * h + 1];
-            pgm += ga * (w[0] * f0.x + w[1] * f1.x + w[2] * f2.x + w[3] * f3.x);
-            pgm += gb * (w[0] * f0.y + w[1] * f1.y + w[2] * f2.y + w[3] * f3.y);
-            pgy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
-            pgy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
-            pgx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
-            pgx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
+          for (int k = 0; k < 4; ++k) {
+            const float2 lo = Vec<T>::unpack(xv[k].x), hi = Vec<T>::unpack(xv[k].y);
+            d[k] = gv.x * lo.x + gv.y * lo.y + gv.z * hi.x + gv.w * hi.y;
           }
+          float pgm = w[0] * d[0] + w[1] * d[1] + w[2] * d[2] + w[3] * d[3];
+          float pgy = m * (fx * (d[3] - d[1]) + (1.f - fx) * (d[2] - d[0]));
+          float pgx = m * (fy * (d[3] - d[2]) + (1.f - fy) * (d[1] - d[0]));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float wk = w[k] * m;
-            if (wk != 0.f)
-              red_v4(a.gi32 + (long long)ci[k] * g.C + cslab, wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
+            if (wk != 0.f) red_v4(a.gi32 + eo[k], wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
           }
-          pgy *= m;
-          pgx *= m;
 #pragma unroll
           for (int sh = 1; sh < 8; sh <<= 1) {
             pgy += __shfl_xor_sync(0xffffffffu, pgy, sh);
@@ -781,20 +776,15 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           for (int k = 0; k < 4; ++k)
             xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + (long long)ci[k] * g.C + c_abs))
                                    : make_uint2(0, 0);
-          const float gvv[4] = {gv.x, gv.y, gv.z, gv.w};
-          float pgy = 0.f, pgx = 0.f, pgm = 0.f;
+          float d[4];  // per corner: sum over the lane's 4 channels of gcol * x
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float2 f0 = Vec<T>::unpack((&xv[0].x)[h]), f1 = Vec<T>::unpack((&xv[1].x)[h]);
-            const float2 f2 = Vec<T>::unpack((&xv[2].x)[h]), f3 = Vec<T>::unpack((&xv[3].x)[h]);
-            const float ga = gvv[2 * h], gb = gvv[2 * h + 1];
-            pgm += ga * (w[0] * f0.x + w[1] * f1.x + w[2] * f2.x + w[3] * f3.x);
-            pgm += gb * (w[0] * f0.y + w[1] * f1.y + w[2] * f2.y + w[3] * f3.y);
-            pgy += ga * (fx * (f3.x - f1.x) + (1.f - fx) * (f2.x - f0.x));
-            pgy += gb * (fx * (f3.y - f1.y) + (1.f - fx) * (f2.y - f0.y));
-            pgx += ga * (fy * (f3.x - f2.x) + (1.f - fy) * (f1.x - f0.x));
-            pgx += gb * (fy * (f3.y - f2.y) + (1.f - fy) * (f1.y - f0.y));
+          for (int k = 0; k < 4; ++k) {
+            const float2 lo = Vec<T>::unpack(xv[k].x), hi = Vec<T>::unpack(xv[k].y);
+            d[k] = gv.x * lo.x + gv.y * lo.y + gv.z * hi.x + gv.w * hi.y;
           }
+          float pgm = w[0] * d[0] + w[1] * d[1] + w[2] * d[2] + w[3] * d[3];
+          float pgy = fx * (d[3] - d[1]) + (1.f - fx) * (d[2] - d[0]);
+          float pgx = fy * (d[3] - d[2]) + (1.f - fy) * (d[1] - d[0]);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float wk = w[k] * m;
@@ -1244,7 +1234,9 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
     a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
     a.b_stages = 4;
-    const int sw = g.cpo % 32 == 0 ? 32 : 16;  // epilogue slab width (see the kernel)
+    // epilogue slab width (see the kernel); the 32-channel variant addresses
+    // the input and grad_input with 32-bit element offsets
+    const int sw = (g.cpo % 32 == 0 && (long long)g.B * g.H * g.W * g.C < (1LL << 31)) ? 32 : 16;
     while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) --a.b_stages;
     if (dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
     a.idesc = idesc_f16(BM, 64, bf16);
