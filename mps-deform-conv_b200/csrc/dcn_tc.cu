@@ -128,14 +128,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
 
   if (warp < NPROD_WARPS) {
     // ------------------------------------------------ producers
-    const int r = warp * 8 + (lane >> 2), cq = lane & 3;
-    const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
+    const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
+    const PixelCtx pc[2] = {pixel_ctx(g, (long long)tile * BM + r0), pixel_ctx(g, (long long)tile * BM + r0 + 4)};
     uint8_t* cols_tile = a.cols ? static_cast<uint8_t*>(a.cols) +
                                       ((size_t)grp * gridDim.x + tile) * a.nkc * (size_t)A_STAGE_BYTES
                                 : nullptr;
     Ring ring{0, S, 0u};
     const bool ok = gather_run<T>(
-        g, xh, off, msk, pc, r, cq, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
+        g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
         [&](int i, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
           t = smem + L.a + s * A_STAGE_BYTES;
           gt = cols_tile ? cols_tile + (size_t)i * A_STAGE_BYTES : nullptr;
@@ -301,8 +301,9 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   if (g.cpo % 8 != 0) return false;                  // 16-byte vectors inside one offset group
   if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N per MMA: Cog or Cog/2, multiple of 16
   if (pick_stages(g.Cog) < 2) return false;
-  // the gather addresses one image's input and offset planes with 32-bit offsets
-  if ((long long)g.H * g.W * g.C >= (1LL << 31) || (long long)g.OG * 2 * g.T * g.HWo >= (1LL << 31)) return false;
+  // the gather addresses the input and offset tensors with 32-bit element offsets
+  if ((long long)g.B * g.H * g.W * g.C >= (1LL << 31) || (long long)g.B * g.OG * 2 * g.T * g.HWo >= (1LL << 31))
+    return false;
   return true;
 }
 

@@ -136,12 +136,13 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
 
   if (warp < W_NPROD_WARPS) {
     // -------------------------------------------- col-tile producers
-    const int r = warp * 8 + (lane >> 2), cq = lane & 3;
+    const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
     bool ok = true;
     Ring ring{0, BS, 0u};  // continues across the CTA's pixel tiles
     for (int li = 0; li < nt && ok; ++li) {
-      const PixelCtx pc = pixel_ctx(g, (long long)(t0 + li) * BM + r);
-      ok = gather_run<T>(g, xh, off, msk, pc, r, cq, grp * g.Cig, k0, nk, ring, abort_flag, a.status, ST_W_PROD,
+      const PixelCtx pc[2] = {pixel_ctx(g, (long long)(t0 + li) * BM + r0),
+                              pixel_ctx(g, (long long)(t0 + li) * BM + r0 + 4)};
+      ok = gather_run<T>(g, xh, off, msk, pc, r0, q, grp * g.Cig, k0, nk, ring, abort_flag, a.status, ST_W_PROD,
                          [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
                            t = smem + L.b + s * A_STAGE_BYTES;
                            gt = nullptr;

@@ -42,11 +42,9 @@ template <> struct Vec<__half> {
 
 // ---------------------------------------------------------------- gather
 // A producer warp owns 8 consecutive pixel rows (8*warp .. 8*warp+7) of a
-// 128-row operand tile [pixels][64 channels].  Lane l works on row
-// 8*warp + l/4 and on the 16-byte channel chunks (l%4) and (l%4)+4 of the
-// K chunk, so one load instruction covers 8 pixels x 64 contiguous bytes of a
-// corner (whole 32-byte sectors).  The offset/mask values of the next K chunk
-// are loaded while the current chunk's corners are in flight.
+// 128-row operand tile [pixels][64 channels] (lane mapping: gather_run).
+// The offset/mask values of the next K chunk are loaded while the current
+// chunk's corners are in flight.
 constexpr int GATHER_WARPS = 16;
 constexpr int GATHER_THREADS = GATHER_WARPS * 32;
 
@@ -238,90 +236,92 @@ __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCt
 }
 
 // One producer thread's share of a run of K chunks for one pixel tile (gather
-// order above): per chunk it waits for its stage to be free, gathers 2 x 16
-// bytes of 4 corners, blends, and writes its two 16-byte chunks of row r into
-// the swizzled tile.  The sampling point and the offset / mask loads are
-// reused while consecutive chunks share the tap and the offset groups.
-// `ring` is the stage ring position (advanced once per chunk);
+// order above).  A producer warp owns 8 rows of the 128-row operand tile;
+// lane l works on rows r0 = 8*warp + l/8 and r0 + 4 and on the 16-byte
+// channel chunk q = l%8 of the K chunk, so one load instruction covers 4
+// pixels x 128 contiguous bytes of a corner (whole cache lines).  Per chunk
+// it waits for its stage to be free, gathers 16 bytes of the 4 corners of
+// both pixels, blends, and writes its chunk of both rows into the swizzled
+// tile.  The sampling points and the offset / mask loads are reused while
+// consecutive chunks share the tap and the offset group.  `ring` is the
+// stage ring position (advanced once per chunk);
 // `stage_of(i, s, tile, gtile, empty_bar, full_bar)` gives the shared-memory
 // tile of stage s, the global copy of the i-th tile of the run (or null) and
-// the barriers.  Returns false if a wait expired.  Per image the offset plane
-// (OG*2*T*Ho*Wo elements) and the input plane (H*W*C) are below 2^31.
+// the barriers.  Returns false if a wait expired.  The input (B*H*W*C) and
+// offset (B*OG*2*T*Ho*Wo) tensors hold fewer than 2^31 elements.
 template <typename T, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
-                                           const PixelCtx& pc, int r, int cq, int cbase_grp, int kc0,
+                                           const PixelCtx (&pc)[2], int r0, int q, int cbase_grp, int kc0,
                                            int nk, Ring& ring, volatile int* abort_flag, int* status,
                                            int code, StageFn&& stage_of) {
   const int ncc = g.Cig / BK;
-  const T* __restrict__ ximg = xh + (size_t)pc.img * g.C;
-  const T* __restrict__ offp = off + (size_t)pc.b * g.OG * 2 * g.T * g.HWo + pc.p;
-  const T* __restrict__ mskp = msk ? msk + (size_t)pc.b * g.OG * g.T * g.HWo + pc.p : nullptr;
-  auto load = [&](int o, int t) {
+  // 32-bit element offsets of each pixel's image in the input and of its
+  // (image, pixel) in the offset / mask tensors (whole tensors < 2^31 elements)
+  int xo[2], oo[2], mo[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    xo[h] = (int)pc[h].img * g.C;
+    oo[h] = pc[h].b * g.OG * 2 * g.T * g.HWo + pc[h].p;
+    mo[h] = pc[h].b * g.OG * g.T * g.HWo + pc[h].p;
+  }
+  auto load = [&](int h, int o, int t) {
     RawSample<T> rs;
-    const int ob = (o * 2 * g.T + 2 * t) * g.HWo;
-    rs.dy = offp[ob];
-    rs.dx = offp[ob + g.HWo];
-    rs.m = mskp ? mskp[(o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    const int ob = oo[h] + (o * 2 * g.T + 2 * t) * g.HWo;
+    rs.dy = off[ob];
+    rs.dx = off[ob + g.HWo];
+    rs.m = msk ? msk[mo[h] + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
     return rs;
   };
   GatherWalk kw;
   kw.start(g, kc0, ncc);
-  // offset groups of the lane's two vectors (channels cq*8 and cq*8 + 32 of
-  // the chunk) at chunk cc = 0 and at the current chunk
-  OgTrack a0, b0, a, b;
-  a0.set(cbase_grp + cq * 8, g.cpo);
-  b0.set(cbase_grp + cq * 8 + 32, g.cpo);
-  a.set(cbase_grp + kw.cc * BK + cq * 8, g.cpo);
-  b.set(cbase_grp + kw.cc * BK + cq * 8 + 32, g.cpo);
-  RawSample<T> raw0 = load(a.og, kw.t);
-  RawSample<T> raw1 = (b.og == a.og) ? raw0 : load(b.og, kw.t);
-  CornerSet32 cs0, cs1;
-  bool reuse = false;  // cs0 / cs1 already hold this chunk's corners
+  // offset group of the lane's 8-channel vector at chunk cc = 0 and now
+  OgTrack a0, a;
+  a0.set(cbase_grp + q * 8, g.cpo);
+  a.set(cbase_grp + kw.cc * BK + q * 8, g.cpo);
+  RawSample<T> raw[2] = {load(0, a.og, kw.t), load(1, a.og, kw.t)};
+  CornerSet32 cs[2];
+  bool reuse = false;  // cs already holds this chunk's corners
+  const int r1 = r0 + 4;
+  const int o0 = r0 * 128 + ((q ^ (r0 & 7)) << 4), o1 = r1 * 128 + ((q ^ (r1 & 7)) << 4);
   for (int i = 0; i < nk; ++i) {
     if (!reuse) {
-      cs0 = corner_set32(g, pc, raw0, kw.ti, kw.tj);
-      cs1 = (b.og == a.og) ? cs0 : corner_set32(g, pc, raw1, kw.ti, kw.tj);
+      cs[0] = corner_set32(g, pc[0], raw[0], kw.ti, kw.tj);
+      cs[1] = corner_set32(g, pc[1], raw[1], kw.ti, kw.tj);
     }
-    const int c0 = cbase_grp + kw.cc * BK + cq * 8;
-    uint4 v0[4], v1[4];
+    const int c0 = cbase_grp + kw.cc * BK + q * 8;
+    uint4 v[2][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v0[k] = (cs0.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(ximg + cs0.off[k] + c0))
-                                : make_uint4(0, 0, 0, 0);
-      v1[k] = (cs1.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(ximg + cs1.off[k] + c0 + 32))
-                                : make_uint4(0, 0, 0, 0);
-    }
-    // the next chunk: same sampling point, or prefetch its offsets and mask
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        v[h][k] = (cs[h].w[k] != 0.f)
+                      ? __ldg(reinterpret_cast<const uint4*>(xh + (uint32_t)(xo[h] + cs[h].off[k] + c0)))
+                      : make_uint4(0, 0, 0, 0);
+    // the next chunk: same sampling points, or prefetch their offsets and masks
     if (i + 1 < nk) {
-      const int pt = kw.t, pa = a.og, pb = b.og;
+      const int pt = kw.t, pa = a.og;
       kw.next(g, ncc);
-      if (kw.cc == 0) {
-        a = a0;
-        b = b0;
-      } else {
-        a.step64(g.cpo);
-        b.step64(g.cpo);
-      }
-      reuse = kw.t == pt && a.og == pa && b.og == pb;
+      if (kw.cc == 0) a = a0;
+      else a.step64(g.cpo);
+      reuse = kw.t == pt && a.og == pa;
       if (!reuse) {
-        raw0 = load(a.og, kw.t);
-        if (b.og != a.og) raw1 = load(b.og, kw.t);
+        raw[0] = load(0, a.og, kw.t);
+        raw[1] = load(1, a.og, kw.t);
       }
     }
     uint8_t* tile;
     uint8_t* gtile;  // global copy of the tile image, or null
     uint32_t empty_bar, full_bar;
     stage_of(i, ring.s, tile, gtile, empty_bar, full_bar);
-    const uint4 o0v = blend8<T>(v0, cs0.w), o1v = blend8<T>(v1, cs1.w);
-    const int o0 = r * 128 + ((cq ^ (r & 7)) << 4), o1 = r * 128 + (((cq + 4) ^ (r & 7)) << 4);
+    const uint4 b0 = blend8<T>(v[0], cs[0].w), b1 = blend8<T>(v[1], cs[1].w);
     if (gtile) {  // streaming stores: keep L2 for the gather
-      __stcs(reinterpret_cast<uint4*>(gtile + o0), o0v);
-      __stcs(reinterpret_cast<uint4*>(gtile + o1), o1v);
+      __stcs(reinterpret_cast<uint4*>(gtile + o0), b0);
+      __stcs(reinterpret_cast<uint4*>(gtile + o1), b1);
     }
     if (!mbar_wait(empty_bar, ring.ph ^ 1u, abort_flag, status, code)) return false;
-    *reinterpret_cast<uint4*>(tile + o0) = o0v;
-    *reinterpret_cast<uint4*>(tile + o1) = o1v;
+    *reinterpret_cast<uint4*>(tile + o0) = b0;
+    *reinterpret_cast<uint4*>(tile + o1) = b1;
     fence_async_shared();
     mbar_arrive(full_bar);
     ring.next();
