@@ -222,8 +222,9 @@ DCN_API int dcn_deform_conv2d_backward_train(const dcn_conv_desc *desc, const vo
  * has been enqueued on `stream`: work that the callback enqueues on another
  * stream after waiting on an event it records on `stream` sees the final
  * parameter gradients.  On the tensor-core path the callback comes before
- * the input / offset / mask gradient kernels are enqueued, so that work runs
- * alongside them; on the other paths it comes after them.  It is not called
+ * the final layout passes of the input / offset / mask gradients are
+ * enqueued, so that work runs alongside them; on the other paths it comes
+ * after all gradient kernels.  It is not called
  * when the function returns an error before enqueuing anything.  The callback
  * must not call back into this library on the same stream.
  */

@@ -1219,10 +1219,6 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     convert_multi_kernel<T><<<1, 256, 0, st>>>(jobs);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  // grad_weight and grad_bias are final once the work enqueued so far has run:
-  // a caller can start their all-reduce on another stream while the input /
-  // offset / mask gradients are computed below
-  if (ready) ready(user);
   if (need_d) {
     {
       KernelScope ks("weight_t_swizzle", st);
@@ -1258,6 +1254,12 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     kern<<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  // grad_weight and grad_bias are final once the work enqueued so far has run:
+  // a caller can start their all-reduce on another stream now.  It then runs
+  // alongside the final layout passes below, whose small CTAs leave room on
+  // the SMs; beside the gradient GEMM kernels (one CTA per SM) the
+  // collective's blocks would take SMs from them.
+  if (ready) ready(user);
   // ---- finalize
   if (gin) {
     KernelScope ks("grad_input_to_nchw", st);

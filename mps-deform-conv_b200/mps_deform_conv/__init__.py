@@ -46,9 +46,10 @@ def set_training_cache(enabled: bool) -> None:
 
 # Called as hook(grad_weight, grad_bias) during each backward, as soon as those
 # two gradients are enqueued on the current stream (either may be None).  On
-# the tensor-core path the input / offset / mask gradients are enqueued after
-# the hook returns, so work the hook starts on another stream -- typically the
-# data-parallel all-reduce of the parameter gradients -- runs alongside them.
+# the tensor-core path the final layout passes of the input / offset / mask
+# gradients are enqueued after the hook returns, so work the hook starts on
+# another stream -- typically the data-parallel all-reduce of the parameter
+# gradients -- runs alongside them.
 # Work on another stream must wait for an event recorded on the current stream
 # inside the hook, and the caller joins that stream before reading the
 # gradients.  No reference counterpart (its backward returns all gradients at

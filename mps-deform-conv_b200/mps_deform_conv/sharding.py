@@ -12,7 +12,8 @@ holds the two host-side pieces of that scheme:
   GPUs, gloo on CPU).
 * ``OverlappedParamAllReduce`` -- the same all-reduce started from the
   backward's parameter-gradient hook (``set_param_grad_hook``) on a side
-  stream, so it runs while the input / offset / mask gradients are computed.
+  stream, so it runs while the backward finishes the input / offset / mask
+  gradients.
 """
 from __future__ import annotations
 
