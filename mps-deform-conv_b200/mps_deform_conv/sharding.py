@@ -64,8 +64,12 @@ class OverlappedParamAllReduce:
     returns, call ``h.wait()`` before reading the parameter gradients (it makes
     the current stream wait for the side stream; on CPU the reduction already
     ran inside the hook).  The gradients are reduced in place, so the caller
-    keeps them alive until ``wait()``.  Every rank must run the same layers in
-    the same order, as for any collective.
+    keeps them alive until ``wait()`` and reads them only after it: with
+    ``loss.backward()`` the parameters' ``.grad`` must be None before the
+    backward (``zero_grad(set_to_none=True)``, the default), since autograd
+    would otherwise add the new gradient into the old one on the current
+    stream before the side-stream reduction ends.  Every rank must run the same
+    layers in the same order, as for any collective.
     """
 
     def __init__(self, group=None, average: bool = False, stream=None):
