@@ -210,6 +210,39 @@ DCN_API int dcn_deform_conv2d_backward_train(const dcn_conv_desc *desc, const vo
                                              void *stream);
 
 /* ---------------------------------------------------------------------
+ * DCNv2 offset/mask head, fused.  No reference counterpart: the reference's
+ * ModulatedDeformConv2d (mps_deform_conv/__init__.py:500-511) slices the
+ * output of its offset convolution into offsets and mask logits, applies a
+ * sigmoid to the logits, and makes both contiguous before the operator runs.
+ * Here the operator reads that output in place:
+ *   offset_mask [B][OG*T*3][Ho][Wo]: channels [0, 2*OG*T) are the offsets
+ *   (layout as `offset` above), channels [2*OG*T, 3*OG*T) are mask logits;
+ *   the mask is sigmoid(logit), computed in fp32 inside the kernels.
+ * desc->use_mask must be 1.  dcn_head_supported() says whether a problem can
+ * take this layout (fp16/bf16 on the tensor-core kernels, offset groups of a
+ * multiple of 32 channels, input below 2^31 elements); other problems return
+ * DCN_ERR_UNSUPPORTED and use the plain entry points.  Workspace: the
+ * dcn_forward_workspace_size / dcn_backward_workspace_size of the same
+ * descriptor.  `saved` (dcn_saved_state_bytes, or NULL) works as in the
+ * training pair.  The backward writes grad_offset_mask [B][OG*T*3][Ho][Wo]:
+ * the offset gradients and the gradients of the mask logits
+ * (m * (1 - m) * dL/dm); NULL gradient pointers are skipped.
+ */
+DCN_API int dcn_head_supported(const dcn_conv_desc *desc);
+DCN_API int dcn_deform_conv2d_forward_head(const dcn_conv_desc *desc, const void *input,
+                                           const void *weight, const void *offset_mask,
+                                           const void *bias, void *output, void *saved,
+                                           size_t saved_bytes, void *workspace,
+                                           size_t workspace_bytes, void *stream);
+DCN_API int dcn_deform_conv2d_backward_head(const dcn_conv_desc *desc, const void *grad_output,
+                                            const void *input, const void *weight,
+                                            const void *offset_mask, const void *saved,
+                                            size_t saved_bytes, void *grad_input,
+                                            void *grad_weight, void *grad_offset_mask,
+                                            void *grad_bias, void *workspace,
+                                            size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
  * Backward with a parameter-gradient callback, for overlapping the
  * data-parallel all-reduce of grad_weight / grad_bias with the rest of the
  * backward.  No reference counterpart: the reference's backward

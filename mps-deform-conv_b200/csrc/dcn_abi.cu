@@ -503,6 +503,88 @@ int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc* d, const void* grad_
                        stream, params_ready, user_data);
 }
 
+// ---------------------------------------------------------------- DCNv2 head layout
+// offset_mask [B][OG*T*3][Ho][Wo]: offsets in channels [0, 2*OG*T), mask
+// logits in [2*OG*T, 3*OG*T); the kernels read both in place and apply the
+// sigmoid.  Tensor-core path with 32-channel dgrad slabs only.
+static Geom head_geom(const dcn_conv_desc& d) {
+  Geom g = make_geom(d);
+  g.off_bs = 3LL * g.OG * g.T * g.HWo;
+  g.msk_bs = g.off_bs;
+  g.msk_logit = 1;
+  return g;
+}
+
+int dcn_head_supported(const dcn_conv_desc* d) {
+  if (validate(d) != DCN_OK || !d->use_mask) return 0;
+  const Geom g = head_geom(*d);
+  return (tc_backward_supported(*d, g) && g.cpo % 32 == 0 && (long long)g.B * g.H * g.W * g.C < (1LL << 31))
+             ? 1
+             : 0;
+}
+
+static int head_check(const dcn_conv_desc* d, const char* fn) {
+  const int r = validate(d);
+  if (r != DCN_OK) return r;
+  if (!dcn_head_supported(d))
+    return fail(DCN_ERR_UNSUPPORTED,
+                "%s: the DCNv2 head layout needs use_mask, fp16/bf16, per-group channels that the tensor-core "
+                "kernels take and offset groups of a multiple of 32 channels",
+                fn);
+  return DCN_OK;
+}
+
+int dcn_deform_conv2d_forward_head(const dcn_conv_desc* d, const void* input, const void* weight,
+                                   const void* offset_mask, const void* bias, void* output, void* saved,
+                                   size_t saved_bytes, void* workspace, size_t workspace_bytes, void* stream) {
+  int r = head_check(d, "deform_conv2d_forward_head");
+  if (r != DCN_OK) return r;
+  const Geom g = head_geom(*d);
+  if (g.P == 0) return ok();
+  if (!input || !weight || !offset_mask || !output)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (input, weight, offset_mask, output)");
+  const size_t need = tc_forward_workspace(*d, g);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+  if (saved && saved_bytes < saved_layout(g).total)
+    return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
+                saved_bytes);
+  const void* mask = static_cast<const char*>(offset_mask) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
+  cudaError_t e = tc_forward(*d, g, input, weight, offset_mask, mask, bias, output, workspace, saved,
+                             (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward_head");
+}
+
+int dcn_deform_conv2d_backward_head(const dcn_conv_desc* d, const void* grad_output, const void* input,
+                                    const void* weight, const void* offset_mask, const void* saved,
+                                    size_t saved_bytes, void* grad_input, void* grad_weight,
+                                    void* grad_offset_mask, void* grad_bias, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  int r = head_check(d, "deform_conv2d_backward_head");
+  if (r != DCN_OK) return r;
+  const Geom g = head_geom(*d);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (g.P == 0) {  // empty batch: parameter gradients are zero sums
+    cudaError_t e = cudaSuccess;
+    const size_t es = elem_size(d->dtype);
+    if (grad_weight) e = cudaMemsetAsync(grad_weight, 0, es * (size_t)g.Co * g.Cig * g.T, st);
+    if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, es * (size_t)g.Co, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_head");
+  }
+  if (!grad_output || !input || !weight || !offset_mask)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (grad_output, input, weight, offset_mask)");
+  const size_t need = tc_backward_workspace(*d, g);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+  if (saved && saved_bytes < saved_layout(g).total)
+    return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
+                saved_bytes);
+  const void* mask = static_cast<const char*>(offset_mask) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
+  cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset_mask, mask, saved, grad_input, grad_weight,
+                              grad_offset_mask, nullptr, grad_bias, workspace, st, nullptr, nullptr);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_head");
+}
+
 int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void* grad_col,
                                              const void* offset, const void* mask,
                                              void* grad_input, void* stream) {

@@ -46,6 +46,12 @@ struct Geom {
   int Cog;    // Co / G  (output channels per weight group)
   int cpo;    // C / OG  (input channels per offset group)
   long long P;  // B*Ho*Wo
+  // Per-sample strides (elements) of the offset and mask tensors, and whether
+  // the mask holds logits: OG*2*T*Ho*Wo, OG*T*Ho*Wo and 0 for the tensors
+  // above; 3*OG*T*Ho*Wo, 3*OG*T*Ho*Wo and 1 when both are views of one DCNv2
+  // head output [B][OG*T*3][Ho][Wo] (offsets first, then mask logits).
+  long long off_bs, msk_bs;
+  int msk_logit;
 };
 
 inline Geom make_geom(const dcn_conv_desc& d) {
@@ -63,7 +69,16 @@ inline Geom make_geom(const dcn_conv_desc& d) {
   g.Cog = g.Co / g.G;
   g.cpo = g.C / g.OG;
   g.P = (long long)g.B * g.HWo;
+  g.off_bs = (long long)g.OG * 2 * g.T * g.HWo;
+  g.msk_bs = (long long)g.OG * g.T * g.HWo;
+  g.msk_logit = 0;
   return g;
+}
+
+// Mask value of a sample from its stored value: the value itself, or the
+// sigmoid of a stored logit (DCNv2 head layout).
+__device__ __forceinline__ float mask_of(const Geom& g, float v) {
+  return g.msk_logit ? 1.f / (1.f + __expf(-v)) : v;
 }
 
 // Sampling point of a tap: the integer base position (oy*stride - pad +
@@ -95,10 +110,10 @@ __device__ __forceinline__ SamplePos sample_point(const Geom& g, const T* __rest
                                                   int p, float* m) {
   const int oy = p / g.Wo, ox = p - oy * g.Wo;
   const int i = t / g.kw, j = t - i * g.kw;
-  const long long obase = ((long long)(b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + p;
+  const long long obase = (long long)b * g.off_bs + (long long)(o * 2 * g.T + 2 * t) * g.HWo + p;
   const float dy = to_f(offset[obase]);
   const float dx = to_f(offset[obase + g.HWo]);
-  *m = g.use_mask ? to_f(mask[((long long)(b * g.OG + o) * g.T + t) * g.HWo + p]) : 1.0f;
+  *m = g.use_mask ? mask_of(g, to_f(mask[(long long)b * g.msk_bs + (long long)(o * g.T + t) * g.HWo + p])) : 1.0f;
   return sample_pos(oy * g.sh - g.ph + i * g.dh, ox * g.sw - g.pw + j * g.dw, dy, dx);
 }
 

@@ -301,8 +301,9 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   if (g.cpo % 8 != 0) return false;                  // 16-byte vectors inside one offset group
   if (g.Cog % 32 != 0 || g.Cog > 512) return false;  // N per MMA: Cog or Cog/2, multiple of 16
   if (pick_stages(g.Cog) < 2) return false;
-  // the gather addresses the input and offset tensors with 32-bit element offsets
-  if ((long long)g.B * g.H * g.W * g.C >= (1LL << 31) || (long long)g.B * g.OG * 2 * g.T * g.HWo >= (1LL << 31))
+  // the gather addresses the input and offset / mask tensors with 32-bit element offsets
+  if ((long long)g.B * g.H * g.W * g.C >= (1LL << 31) || (long long)g.B * g.off_bs >= (1LL << 31) ||
+      (long long)g.B * g.msk_bs >= (1LL << 31))
     return false;
   return true;
 }

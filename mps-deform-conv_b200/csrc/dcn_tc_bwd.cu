@@ -541,14 +541,16 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       kw.start(g, kc_lo + i);
       const int cbase = grp * g.Cig + kw.cc * BK;
       int tab_o = -1, acc_o = -1;
+      float tab_m = 0.f, acc_m = 0.f;  // mask values of the table's and the running sums' offset group
       float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
       auto flush = [&]() {
         if (acc_o >= 0 && pc.valid) {
-          const long long ob = ((long long)(pc.b * g.OG + acc_o) * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          const long long ob = (long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
           atomicAdd(a.goff32 + ob, run_gy);
           atomicAdd(a.goff32 + ob + g.HWo, run_gx);
-          if (g.use_mask)
-            atomicAdd(a.gmsk32 + ((long long)(pc.b * g.OG + acc_o) * g.T + kw.t) * g.HWo + pc.p, run_gm);
+          if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
+            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p,
+                      g.msk_logit ? run_gm * acc_m * (1.f - acc_m) : run_gm);
         }
         run_gy = run_gx = run_gm = 0.f;
       };
@@ -591,17 +593,18 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
             cidx[k] = v ? (int)((pc.img + c4.idx[k]) * g.C) : 0;  // element offset, B*H*W*C < 2^31
             cw[k] = pc.valid ? cs.w[k] : 0.f;
           }
+          tab_m = pc.valid ? mask_of(g, to_f(raw.m)) : 0.f;
           uint32_t* trow = ws->tab[lane];
           *reinterpret_cast<uint4*>(trow) = make_uint4(cidx[0], cidx[1], cidx[2], cidx[3]);
           *reinterpret_cast<uint4*>(trow + 4) = make_uint4(__float_as_uint(cw[0]), __float_as_uint(cw[1]),
                                                            __float_as_uint(cw[2]), __float_as_uint(cw[3]));
           *reinterpret_cast<uint4*>(trow + 8) =
-              make_uint4(__float_as_uint(c4.fy), __float_as_uint(c4.fx),
-                         __float_as_uint(pc.valid ? to_f(raw.m) : 0.f), cvb);
+              make_uint4(__float_as_uint(c4.fy), __float_as_uint(c4.fx), __float_as_uint(tab_m), cvb);
         }
         if (o != acc_o) {
           flush();
           acc_o = o;
+          acc_m = tab_m;
         }
         __syncwarp();
         // ---- phase 2: 8 lanes per pixel, 4 pixels per step
@@ -697,13 +700,15 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       float cw[4] = {0.f, 0.f, 0.f, 0.f};
       float cfy = 0.f, cfx = 0.f, cm = 0.f;
       uint32_t cvb = 0;
+      // (this variant reads stored mask values; the DCNv2 head layout, whose
+      // mask holds logits, runs on the 32-channel variant only)
       auto flush = [&]() {
         if (acc_o >= 0 && pc.valid) {
-          const long long ob = ((long long)(pc.b * g.OG + acc_o) * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          const long long ob = (long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
           atomicAdd(a.goff32 + ob, run_gy);
           atomicAdd(a.goff32 + ob + g.HWo, run_gx);
           if (g.use_mask)
-            atomicAdd(a.gmsk32 + ((long long)(pc.b * g.OG + acc_o) * g.T + kw.t) * g.HWo + pc.p, run_gm);
+            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p, run_gm);
         }
         run_gy = run_gx = run_gm = 0.f;
       };
@@ -1089,8 +1094,11 @@ BwdWs bwd_ws(const Geom& g, size_t es) {
   L.wdt = o;  o += ws_align(es * (size_t)g.G * nkc * KB * 4096);
   L.acc = o;  // fp32 accumulators, contiguous so one memset clears them
   L.gi32 = o;   o += ws_align(4 * (size_t)g.B * g.H * g.W * g.C);
-  L.goff32 = o; o += ws_align(4 * (size_t)g.B * g.OG * 2 * g.T * g.HWo);
-  L.gmsk32 = o; o += ws_align(4 * (size_t)g.B * g.OG * g.T * g.HWo);
+  // offset / mask gradient accumulators with the strides of the offset and
+  // mask tensors; in the DCNv2 head layout one [B][3*OG*T][HWo] region holds
+  // both (no larger than the two separate regions)
+  L.goff32 = o; o += ws_align(4 * (size_t)g.B * g.off_bs);
+  L.gmsk32 = o; o += g.msk_logit ? 0 : ws_align(4 * (size_t)g.B * g.msk_bs);
   L.gb32 = o;   o += ws_align(4 * (size_t)g.Co);
   L.acc_bytes = o - L.acc;
   L.gwp = o;  // written whole by the wgrad kernels: not cleared
@@ -1120,7 +1128,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   T* wdt = reinterpret_cast<T*>(ws + L.wdt);
   float* gi32 = reinterpret_cast<float*>(ws + L.gi32);
   float* goff32 = reinterpret_cast<float*>(ws + L.goff32);
-  float* gmsk32 = reinterpret_cast<float*>(ws + L.gmsk32);
+  float* gmsk32 = g.msk_logit ? goff32 + (size_t)2 * g.OG * g.T * g.HWo : reinterpret_cast<float*>(ws + L.gmsk32);
   float* gwp = reinterpret_cast<float*>(ws + L.gwp);
   float* gb32 = reinterpret_cast<float*>(ws + L.gb32);
   int* status = tc_status_ptr();
@@ -1276,8 +1284,12 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     auto add = [&](const float* src, void* dst, long long n) {
       if (dst && n > 0) { jobs.src[jobs.n] = src; jobs.dst[jobs.n] = dst; jobs.count[jobs.n] = n; ++jobs.n; }
     };
-    add(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo);
-    if (g.use_mask) add(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo);
+    if (g.msk_logit) {  // DCNv2 head layout: goff is the whole [B][3*OG*T][HWo] gradient
+      add(goff32, goff, (long long)g.B * g.off_bs);
+    } else {
+      add(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo);
+      if (g.use_mask) add(gmsk32, gmsk, (long long)g.B * g.OG * g.T * g.HWo);
+    }
     if (jobs.n > 0) {
       KernelScope ks("f32_convert_multi", st);
       convert_multi_kernel<T><<<148 * 16, 256, 0, st>>>(jobs);

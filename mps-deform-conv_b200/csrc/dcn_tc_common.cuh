@@ -68,7 +68,8 @@ __device__ __forceinline__ PixelCtx pixel_ctx(const Geom& g, long long pix) {
 }
 
 // Offset and mask values of one (pixel, offset group, tap), kept in the
-// storage type so that the loads stay in flight until the values are used.
+// storage type so that the loads stay in flight until the values are used
+// (the mask as stored: a logit in the DCNv2 head layout, see mask_of).
 template <typename T>
 struct RawSample {
   T dy, dx, m;
@@ -79,44 +80,11 @@ __device__ __forceinline__ RawSample<T> load_raw(const Geom& g, const T* __restr
                                                  const T* __restrict__ msk, const PixelCtx& pc, int o,
                                                  int t) {
   RawSample<T> r;
-  const long long ob = ((long long)(pc.b * g.OG + o) * 2 * g.T + 2 * t) * g.HWo + pc.p;
+  const long long ob = (long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * t) * g.HWo + pc.p;
   r.dy = off[ob];
   r.dx = off[ob + g.HWo];
-  r.m = msk ? msk[((long long)(pc.b * g.OG + o) * g.T + t) * g.HWo + pc.p] : from_f<T>(1.f);
+  r.m = msk ? msk[(long long)pc.b * g.msk_bs + (long long)(o * g.T + t) * g.HWo + pc.p] : from_f<T>(1.f);
   return r;
-}
-
-// The four bilinear corners of a sample: element offsets of channel 0 of each
-// corner pixel in the channels-last input, and weights including the mask
-// (zero for invalid corners, samples outside (-1,H)x(-1,W), invalid pixels).
-// Sampling point as in the reference (deform_conv2d_mps.mm:160-168).
-struct CornerSet {
-  long long base[4];
-  float w[4];
-};
-
-template <typename T>
-__device__ __forceinline__ CornerSet corner_set(const Geom& g, const PixelCtx& pc, const RawSample<T>& r,
-                                                int ti, int tj) {
-  CornerSet cs;
-  const SamplePos sp = sample_pos(pc.y0 + ti * g.dh, pc.x0 + tj * g.dw, to_f(r.dy), to_f(r.dx));
-  const Corners c = corners_of(sp, g.H, g.W);
-  const float m = pc.valid ? to_f(r.m) : 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    cs.w[k] = c.w[k] * m;
-    cs.base[k] = (pc.img + c.idx[k]) * g.C;
-  }
-  return cs;
-}
-
-template <typename T>
-__device__ __forceinline__ void load_corners(const T* __restrict__ xh, const CornerSet& cs, int c_abs,
-                                             uint4 (&v)[4]) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    v[k] = (cs.w[k] != 0.f) ? __ldg(reinterpret_cast<const uint4*>(xh + cs.base[k] + c_abs))
-                            : make_uint4(0, 0, 0, 0);
 }
 
 // sum_k w[k] * v[k] over 8 channels as a packed 16-bit FMA chain (two
@@ -226,7 +194,7 @@ __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCt
   CornerSet32 cs;
   const SamplePos sp = sample_pos(pc.y0 + ti * g.dh, pc.x0 + tj * g.dw, to_f(r.dy), to_f(r.dx));
   const Corners c = corners_of(sp, g.H, g.W);
-  const float m = pc.valid ? to_f(r.m) : 0.f;
+  const float m = pc.valid ? mask_of(g, to_f(r.m)) : 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     cs.w[k] = c.w[k] * m;
@@ -248,7 +216,7 @@ __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCt
 // `stage_of(i, s, tile, gtile, empty_bar, full_bar)` gives the shared-memory
 // tile of stage s, the global copy of the i-th tile of the run (or null) and
 // the barriers.  Returns false if a wait expired.  The input (B*H*W*C) and
-// offset (B*OG*2*T*Ho*Wo) tensors hold fewer than 2^31 elements.
+// offset / mask tensors (B * per-sample stride) hold fewer than 2^31 elements.
 template <typename T, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
@@ -262,8 +230,8 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     xo[h] = (int)pc[h].img * g.C;
-    oo[h] = pc[h].b * g.OG * 2 * g.T * g.HWo + pc[h].p;
-    mo[h] = pc[h].b * g.OG * g.T * g.HWo + pc[h].p;
+    oo[h] = pc[h].b * (int)g.off_bs + pc[h].p;
+    mo[h] = pc[h].b * (int)g.msk_bs + pc[h].p;
   }
   auto load = [&](int h, int o, int t) {
     RawSample<T> rs;

@@ -340,6 +340,104 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
   return {gin, gw, goff, gm, gb};
 }
 
+// ---------------------------------------------------------------- DCNv2 head layout
+// offset_mask [B][3*OG*T][Ho][Wo] as ModulatedDeformConv2d's offset convolution
+// produces it (offsets, then mask logits); no reference counterpart (the
+// reference slices it and applies the sigmoid in Python, __init__.py:500-511).
+dcn_conv_desc head_desc(const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset_mask,
+                        int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                        int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps) {
+  TORCH_CHECK(weight.dim() == 4, "weight must be 4-D");
+  dcn_conv_desc d = make_desc(input, weight.size(0), weight.size(2), weight.size(3), stride_h, stride_w, pad_h,
+                              pad_w, dilation_h, dilation_w, n_weight_grps, n_offset_grps, true);
+  TORCH_CHECK(weight.size(1) * n_weight_grps == input.size(1), "weight in_channels (", weight.size(1),
+              ") x n_weight_grps (", n_weight_grps, ") must equal in_channels (", input.size(1), ")");
+  auto [oh, ow] = out_size(d);
+  const int64_t ch = 3 * n_offset_grps * weight.size(2) * weight.size(3);
+  TORCH_CHECK(offset_mask.dim() == 4 && offset_mask.size(0) == d.batch && offset_mask.size(1) == ch &&
+                  offset_mask.size(2) == oh && offset_mask.size(3) == ow,
+              "offset_mask has shape ", offset_mask.sizes(), ", expected (", d.batch, ", ", ch, ", ", oh, ", ", ow,
+              ")");
+  return d;
+}
+
+bool head_supported(const at::Tensor& input, const at::Tensor& weight, int64_t stride_h, int64_t stride_w,
+                    int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w, int64_t n_weight_grps,
+                    int64_t n_offset_grps) {
+  if (weight.dim() != 4) return false;
+  dcn_conv_desc d = make_desc(input, weight.size(0), weight.size(2), weight.size(3), stride_h, stride_w, pad_h,
+                              pad_w, dilation_h, dilation_w, n_weight_grps, n_offset_grps, true);
+  return dcn_head_supported(&d) != 0;
+}
+
+std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_head(
+    const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset_mask, const at::Tensor& bias,
+    int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+    int64_t n_weight_grps, int64_t n_offset_grps, bool keep_saved) {
+  TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
+  check_cuda(weight, "weight", input);
+  check_cuda(offset_mask, "offset_mask", input);
+  const bool has_bias = bias.defined() && bias.numel() > 0;
+  if (has_bias) check_cuda(bias, "bias", input);
+  c10::cuda::CUDAGuard guard(input.device());
+  dcn_conv_desc d = head_desc(input, weight, offset_mask, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                              n_weight_grps, n_offset_grps);
+  if (has_bias) TORCH_CHECK(bias.numel() == weight.size(0), "bias must have out_channels elements");
+  auto [oh, ow] = out_size(d);
+  auto x = input.contiguous(), w = weight.contiguous(), om = offset_mask.contiguous();
+  auto b = has_bias ? bias.contiguous() : at::Tensor();
+  auto out = at::empty({d.batch, d.out_channels, oh, ow}, input.options());
+  const size_t sbytes = keep_saved ? dcn_saved_state_bytes(&d) : 0;
+  auto saved = at::empty({(int64_t)sbytes}, input.options().dtype(at::kByte));
+  auto ws = workspace(dcn_forward_workspace_size(&d), input);
+  check_status(dcn_deform_conv2d_forward_head(&d, x.data_ptr(), w.data_ptr(), om.data_ptr(),
+                                              has_bias ? b.data_ptr() : nullptr, out.data_ptr(),
+                                              sbytes ? saved.data_ptr() : nullptr, sbytes, ws.data_ptr(),
+                                              (size_t)ws.numel(), stream_of(input)));
+  return {out, saved};
+}
+
+// output_mask: (input, weight, offset_mask, bias)
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_conv2d_backward_head(
+    const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset_mask,
+    const at::Tensor& bias, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+    int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps, std::vector<bool> output_mask,
+    const std::optional<at::Tensor>& saved_opt) {
+  TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
+  check_cuda(grad_output, "grad_output", input);
+  check_cuda(weight, "weight", input);
+  check_cuda(offset_mask, "offset_mask", input);
+  const bool has_bias = bias.defined() && bias.numel() > 0;
+  if (output_mask.size() < 4) output_mask.resize(4, true);
+  c10::cuda::CUDAGuard guard(input.device());
+  dcn_conv_desc d = head_desc(input, weight, offset_mask, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                              n_weight_grps, n_offset_grps);
+  auto [oh, ow] = out_size(d);
+  TORCH_CHECK(grad_output.dim() == 4 && grad_output.size(0) == d.batch && grad_output.size(1) == d.out_channels &&
+                  grad_output.size(2) == oh && grad_output.size(3) == ow,
+              "grad_output has shape ", grad_output.sizes(), ", expected (", d.batch, ", ", d.out_channels, ", ", oh,
+              ", ", ow, ")");
+  auto go = grad_output.contiguous(), x = input.contiguous(), w = weight.contiguous(), om = offset_mask.contiguous();
+  at::Tensor gin, gw, gom, gb;
+  if (output_mask[0]) gin = at::empty_like(x);
+  if (output_mask[1]) gw = at::empty_like(w);
+  if (output_mask[2]) gom = at::empty_like(om);
+  if (output_mask[3] && has_bias) gb = at::empty({d.out_channels}, input.options());
+  auto ws = workspace(dcn_backward_workspace_size(&d), input);
+  auto ptr = [](const at::Tensor& t) -> void* { return t.defined() ? t.data_ptr() : nullptr; };
+  const at::Tensor saved = saved_opt.has_value() ? *saved_opt : at::Tensor();
+  const bool has_saved = saved.defined() && saved.numel() > 0;
+  if (has_saved)
+    TORCH_CHECK(saved.is_cuda() && saved.device() == input.device() && saved.scalar_type() == at::kByte &&
+                    saved.is_contiguous(),
+                "saved state must be a contiguous uint8 tensor on the input's device");
+  check_status(dcn_deform_conv2d_backward_head(
+      &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), om.data_ptr(), has_saved ? saved.data_ptr() : nullptr,
+      has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw), ptr(gom), ptr(gb), ws.data_ptr(),
+      (size_t)ws.numel(), stream_of(input)));
+  return {gin, gw, gom, gb};
+}
+
 bool uses_tensor_cores(const at::Tensor& input, const at::Tensor& weight, int64_t stride_h,
                        int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
                        int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps,
@@ -377,6 +475,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("deform_conv2d_forward_train", &deform_conv2d_forward_train,
         "Forward that also returns the device state its backward reuses: (output, saved)");
   m.def("uses_tensor_cores", &uses_tensor_cores, "True when the tcgen05 kernels run this problem");
+  m.def("head_supported", &head_supported, "True when the fused DCNv2 offset/mask head layout runs this problem");
+  m.def("deform_conv2d_forward_head", &deform_conv2d_forward_head,
+        "Forward reading offsets and mask logits in place from the DCNv2 head output: (output, saved)");
+  m.def("deform_conv2d_backward_head", &deform_conv2d_backward_head,
+        "Backward of forward_head: (grad_input, grad_weight, grad_offset_mask, grad_bias)",
+        py::arg("grad_output"), py::arg("input"), py::arg("weight"), py::arg("offset_mask"), py::arg("bias"),
+        py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"), py::arg("pad_w"), py::arg("dilation_h"),
+        py::arg("dilation_w"), py::arg("n_weight_grps"), py::arg("n_offset_grps"),
+        py::arg("output_mask") = std::vector<bool>{true, true, true, true}, py::arg("saved") = py::none());
   m.def("device_status", &device_status, "Raise if a kernel's bounded wait expired");
   m.def("abi_version", &dcn_abi_version);
 }

@@ -44,6 +44,19 @@ def set_training_cache(enabled: bool) -> None:
     _training_cache = bool(enabled)
 
 
+# ModulatedDeformConv2d reads its offset convolution's output in place (offsets
+# and mask logits, sigmoid inside the kernels) when the problem allows it, or
+# slices it and applies the sigmoid in PyTorch first as the reference does
+# (mps_deform_conv/__init__.py:500-511).
+_head_fusion = True
+
+
+def set_head_fusion(enabled: bool) -> None:
+    """Fuse (True, default) or compose (False) ModulatedDeformConv2d's offset/mask head."""
+    global _head_fusion
+    _head_fusion = bool(enabled)
+
+
 # Called as hook(grad_weight, grad_bias) during each backward, as soon as those
 # two gradients are enqueued on the current stream (either may be None).  On
 # the tensor-core path the final layout passes of the input / offset / mask
@@ -271,6 +284,40 @@ class _DeformConv2dFunction(torch.autograd.Function):
                 None, None, None, grad_mask, None, None, None)
 
 
+class _DeformConv2dHeadFunction(torch.autograd.Function):
+    """deform_conv2d reading offsets and mask logits in place from a DCNv2 head
+    output [B, 3*og*kh*kw, Ho, Wo] (offsets first); the mask is the sigmoid of
+    the logits.  Its backward returns the gradient of that head output."""
+
+    @staticmethod
+    def forward(ctx, input, offset_mask, weight, bias, stride, padding, dilation, n_weight_grps, n_offset_grps):
+        lib = _get_lib()
+        bias_t = bias if bias is not None else torch.empty(0, device=input.device, dtype=input.dtype)
+        keep = _training_cache and ctx.needs_input_grad[2]
+        output, saved = lib.deform_conv2d_forward_head(
+            input, weight, offset_mask, bias_t, stride[0], stride[1], padding[0], padding[1],
+            dilation[0], dilation[1], n_weight_grps, n_offset_grps, keep)
+        ctx.save_for_backward(input, offset_mask, weight, saved)
+        ctx.geom = (stride, padding, dilation, n_weight_grps, n_offset_grps)
+        ctx.bias_exists = bias is not None
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        input, offset_mask, weight, saved = ctx.saved_tensors
+        (sh, sw), (ph, pw), (dh, dw), n_weight_grps, n_offset_grps = ctx.geom
+        needs = ctx.needs_input_grad
+        bias_t = (torch.empty(weight.size(0), device=input.device, dtype=input.dtype) if ctx.bias_exists
+                  else torch.empty(0, device=input.device, dtype=input.dtype))
+        output_mask = [bool(needs[0]), bool(needs[2]), bool(needs[1]), bool(ctx.bias_exists and needs[3])]
+        grad_input, grad_weight, grad_offset_mask, grad_bias = _get_lib().deform_conv2d_backward_head(
+            grad_output, input, weight, offset_mask, bias_t, sh, sw, ph, pw, dh, dw, n_weight_grps,
+            n_offset_grps, output_mask, saved if saved.numel() > 0 else None)
+        if _param_grad_hook is not None:  # no overlap on this path: called once all gradients are enqueued
+            _param_grad_hook(grad_weight, grad_bias)
+        return grad_input, grad_offset_mask, grad_weight, grad_bias, None, None, None, None, None
+
+
 def deform_conv2d(
     input: Tensor,
     offset: Tensor,
@@ -418,10 +465,23 @@ class ModulatedDeformConv2d(nn.Module):
         nn.init.zeros_(self.offset_conv.weight)
         nn.init.zeros_(self.offset_conv.bias)
 
+    def _fused_head(self, input: Tensor, offset_mask: Tensor) -> bool:
+        if not (_head_fusion and input.is_cuda and input.dim() == 4 and
+                input.dtype == offset_mask.dtype == self.weight.dtype and
+                (self.bias is None or self.bias.dtype == input.dtype)):
+            return False
+        return bool(_get_lib().head_supported(
+            input, self.weight, self.stride[0], self.stride[1], self.padding[0], self.padding[1],
+            self.dilation[0], self.dilation[1], self.groups, self.offset_groups))
+
     def forward(self, input: Tensor) -> Tensor:
         kernel_h, kernel_w = self.kernel_size
         offset_channels = 2 * kernel_h * kernel_w * self.offset_groups
         offset_mask = self.offset_conv(input)
+        if self._fused_head(input, offset_mask):
+            return _DeformConv2dHeadFunction.apply(
+                input, offset_mask, self.weight, self.bias, tuple(self.stride), tuple(self.padding),
+                tuple(self.dilation), self.groups, self.offset_groups)
         offset = offset_mask[:, :offset_channels]
         mask = torch.sigmoid(offset_mask[:, offset_channels:])
         return deform_conv2d(
@@ -436,4 +496,4 @@ def is_available() -> bool:
 
 
 __all__ = ["deform_conv2d", "DeformConv2d", "ModulatedDeformConv2d", "is_available", "__version__",
-           "set_training_cache", "set_param_grad_hook"]
+           "set_training_cache", "set_param_grad_hook", "set_head_fusion"]

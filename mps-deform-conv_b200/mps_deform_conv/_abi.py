@@ -66,6 +66,10 @@ SIGNATURES = {
                                                         _V, _SZ, _V]),
     "dcn_deform_conv2d_backward_overlap": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V,
                                                           _V, _SZ, _V, PARAMS_READY_FN, _V]),
+    "dcn_head_supported": (ctypes.c_int, [_D]),
+    "dcn_deform_conv2d_forward_head": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
+    "dcn_deform_conv2d_backward_head": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V, _SZ,
+                                                       _V]),
     "dcn_device_status": (ctypes.c_int, [_V]),
     "dcn_uses_tensor_cores": (ctypes.c_int, [_D]),
 }

@@ -93,6 +93,30 @@ def test_forward_rejects_null_and_small_workspace_without_launching():
     assert rc == _abi.DCN_ERR_WORKSPACE
 
 
+def test_head_layout_support_query_and_rejection_without_launching():
+    """The fused DCNv2 head layout is a tensor-core-only path: the query is a
+    host computation, and an unsupported problem is rejected before any
+    pointer is touched."""
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    ok = _desc(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1),
+               use_mask=True)
+    assert lib.dcn_head_supported(ctypes.byref(ok)) == 1
+    for kw in (dict(dtype=_abi.DCN_FLOAT32),           # SIMT path
+               dict(n_offset_grps=8),                   # 8 channels per offset group: 16-channel dgrad slabs
+               dict(use_mask=False)):                   # the head layout carries a mask
+        base = dict(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3),
+                    padding=(1, 1), use_mask=True)
+        base.update(kw)
+        bad = _desc(**base)
+        assert lib.dcn_head_supported(ctypes.byref(bad)) == 0
+        rc = lib.dcn_deform_conv2d_forward_head(ctypes.byref(bad), ctypes.c_void_p(16), ctypes.c_void_p(16),
+                                                ctypes.c_void_p(16), None, ctypes.c_void_p(16), None, 0, None, 0,
+                                                None)
+        assert rc == _abi.DCN_ERR_UNSUPPORTED
+        assert "head layout" in lib.dcn_last_error().decode()
+
+
 def test_torch_extension_imports():
     import mps_deform_conv
     lib = mps_deform_conv._get_lib()
