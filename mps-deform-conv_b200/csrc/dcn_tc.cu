@@ -82,7 +82,8 @@ struct FwdArgs {
   uint32_t tmem_cols;
 };
 
-template <typename T>
+// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout)
+template <typename T, bool LOGIT>
 __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
                                       ((size_t)grp * gridDim.x + tile) * a.nkc * (size_t)A_STAGE_BYTES
                                 : nullptr;
     Ring ring{0, S, 0u};
-    const bool ok = gather_run<T>(
+    const bool ok = gather_run<T, LOGIT>(
         g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
         [&](int i, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
           t = smem + L.a + s * A_STAGE_BYTES;
@@ -407,13 +408,13 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   a.tmem_cols = tmem_cols_for(g.Cog);
   const FwdSmem SL = fwd_smem_layout(g.Cog, a.stages);
   const int smem = (int)SL.total + 1024;
-  if ((e = cudaFuncSetAttribute(dcn_fwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smem)) != cudaSuccess)
+  auto kern = g.msk_logit ? dcn_fwd_tc_kernel<T, true> : dcn_fwd_tc_kernel<T, false>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
     return e;
   dim3 grid((unsigned)((g.P + BM - 1) / BM), (unsigned)g.G);
   {
     KernelScope ks("dcn_fwd_tc", st);
-    dcn_fwd_tc_kernel<T><<<grid, NTHREADS, smem, st>>>(a);
+    kern<<<grid, NTHREADS, smem, st>>>(a);
   }
   return cudaGetLastError();
 }

@@ -87,7 +87,8 @@ __host__ __device__ inline WgradSmem wgrad_smem(int mh, int a_stages, int b_stag
   return L;
 }
 
-template <typename T>
+// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout)
+template <typename T, bool LOGIT>
 __global__ void __launch_bounds__(W_NTHREADS, 1)
 dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
   extern __shared__ uint8_t smem_raw[];
@@ -142,13 +143,14 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
     for (int li = 0; li < nt && ok; ++li) {
       const PixelCtx pc[2] = {pixel_ctx(g, (long long)(t0 + li) * BM + r0),
                               pixel_ctx(g, (long long)(t0 + li) * BM + r0 + 4)};
-      ok = gather_run<T>(g, xh, off, msk, pc, r0, q, grp * g.Cig, k0, nk, ring, abort_flag, a.status, ST_W_PROD,
-                         [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
-                           t = smem + L.b + s * A_STAGE_BYTES;
-                           gt = nullptr;
-                           eb = b_empty(s);
-                           fb = b_full(s);
-                         });
+      auto stage_of = [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
+        t = smem + L.b + s * A_STAGE_BYTES;
+        gt = nullptr;
+        eb = b_empty(s);
+        fb = b_full(s);
+      };
+      ok = gather_run<T, LOGIT>(g, xh, off, msk, pc, r0, q, grp * g.Cig, k0, nk, ring, abort_flag, a.status,
+                                ST_W_PROD, stage_of);
     }
     // -------------------------------------------- epilogue: TMEM -> this split's partial gW
     const bool ready = nt > 0 && ok && mbar_wait(d_full, 0, abort_flag, a.status, ST_W_EPI);
@@ -1202,10 +1204,11 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       KernelScope ks("dcn_wgrad_cols_tc", st);
       dcn_wgrad_cols_tc_kernel<T><<<dim3(kgroups, g.G, splits), WC_NTHREADS, csmem, st>>>(c, cols, tmap64);
     } else {
-      if ((e = cudaFuncSetAttribute(dcn_wgrad_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      auto wkern = g.msk_logit ? dcn_wgrad_tc_kernel<T, true> : dcn_wgrad_tc_kernel<T, false>;
+      if ((e = cudaFuncSetAttribute(wkern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
         return e;
       KernelScope ks("dcn_wgrad_tc", st);
-      dcn_wgrad_tc_kernel<T><<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
+      wkern<<<dim3(kgroups, g.G, splits), W_NTHREADS, smem, st>>>(a, tmap);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     {

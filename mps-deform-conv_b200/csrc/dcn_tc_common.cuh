@@ -188,13 +188,16 @@ struct CornerSet32 {
   float w[4];
 };
 
-template <typename T>
+// LOGIT: the mask holds logits (DCNv2 head layout, Geom::msk_logit); a
+// compile-time choice, so the plain layout's producer carries no select.
+template <typename T, bool LOGIT>
 __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCtx& pc, const RawSample<T>& r,
                                                     int ti, int tj) {
   CornerSet32 cs;
   const SamplePos sp = sample_pos(pc.y0 + ti * g.dh, pc.x0 + tj * g.dw, to_f(r.dy), to_f(r.dx));
   const Corners c = corners_of(sp, g.H, g.W);
-  const float m = pc.valid ? mask_of(g, to_f(r.m)) : 0.f;
+  const float mv = to_f(r.m);
+  const float m = pc.valid ? (LOGIT ? 1.f / (1.f + __expf(-mv)) : mv) : 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     cs.w[k] = c.w[k] * m;
@@ -217,7 +220,7 @@ __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCt
 // tile of stage s, the global copy of the i-th tile of the run (or null) and
 // the barriers.  Returns false if a wait expired.  The input (B*H*W*C) and
 // offset / mask tensors (B * per-sample stride) hold fewer than 2^31 elements.
-template <typename T, class StageFn>
+template <typename T, bool LOGIT, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
                                            const T* __restrict__ off, const T* __restrict__ msk,
                                            const PixelCtx (&pc)[2], int r0, int q, int cbase_grp, int kc0,
@@ -254,8 +257,8 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
   const int o0 = r0 * 128 + ((q ^ (r0 & 7)) << 4), o1 = r1 * 128 + ((q ^ (r1 & 7)) << 4);
   for (int i = 0; i < nk; ++i) {
     if (!reuse) {
-      cs[0] = corner_set32(g, pc[0], raw[0], kw.ti, kw.tj);
-      cs[1] = corner_set32(g, pc[1], raw[1], kw.ti, kw.tj);
+      cs[0] = corner_set32<T, LOGIT>(g, pc[0], raw[0], kw.ti, kw.tj);
+      cs[1] = corner_set32<T, LOGIT>(g, pc[1], raw[1], kw.ti, kw.tj);
     }
     const int c0 = cbase_grp + kw.cc * BK + q * 8;
     uint4 v[2][4];
