@@ -228,7 +228,7 @@ DCN_API int dcn_deform_conv2d_backward_train(const dcn_conv_desc *desc, const vo
  * the offset gradients and the gradients of the mask logits
  * (m * (1 - m) * dL/dm); NULL gradient pointers are skipped.
  */
-DCN_API int dcn_head_supported(const dcn_conv_desc *desc);
+DCN_API int dcn_head_supported(const dcn_conv_desc *desc);  /* dcn_ex_supported, head = 1, backward */
 DCN_API int dcn_deform_conv2d_forward_head(const dcn_conv_desc *desc, const void *input,
                                            const void *weight, const void *offset_mask,
                                            const void *bias, void *output, void *saved,
@@ -241,6 +241,52 @@ DCN_API int dcn_deform_conv2d_backward_head(const dcn_conv_desc *desc, const voi
                                             void *grad_weight, void *grad_offset_mask,
                                             void *grad_bias, void *workspace,
                                             size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Memory formats and the DCNv2 head layout, in one pair of entry points.
+ * No reference counterpart (the reference makes every tensor NCHW-contiguous
+ * first, deform_conv2d_mps.mm:684-686).
+ *   input_layout  applies to input and grad_input,
+ *   output_layout applies to output and grad_output:
+ *     DCN_LAYOUT_NCHW   [B][C][H][W] as above;
+ *     DCN_LAYOUT_NHWC   channels-last [B][H][W][C] (PyTorch's channels_last
+ *                       memory format), 16-byte aligned: the gather reads a
+ *                       channels-last input in place, and a channels-last
+ *                       grad_output is already the pixel-major operand of the
+ *                       gradient GEMMs, so the NCHW <-> channels-last passes
+ *                       are skipped.
+ *   head = 1: `offset` is the DCNv2 head output described above and `mask`
+ *             is ignored (grad_offset then receives the head gradient and
+ *             grad_mask is ignored).
+ * offset, mask and their gradients stay NCHW.  With plain options (both NCHW,
+ * no head; or opt == NULL) these calls are the _train pair and every problem
+ * is accepted; otherwise dcn_ex_supported(desc, opt, backward) says whether
+ * the forward (backward = 0) or the backward (1) takes the problem, and the
+ * calls return DCN_ERR_UNSUPPORTED when it does not.  Workspace and `saved`
+ * as in the training pair (with a channels-last input the saved state's input
+ * copy is not used).
+ */
+#define DCN_LAYOUT_NCHW 0
+#define DCN_LAYOUT_NHWC 1
+typedef struct dcn_ex_options {
+  int32_t input_layout;   /* input and grad_input */
+  int32_t output_layout;  /* output and grad_output */
+  int32_t head;           /* 1: offset is a DCNv2 head output [B][OG*T*3][Ho][Wo] */
+  int32_t reserved;       /* 0 */
+} dcn_ex_options;
+DCN_API int dcn_ex_supported(const dcn_conv_desc *desc, const dcn_ex_options *opt, int backward);
+DCN_API int dcn_deform_conv2d_forward_ex(const dcn_conv_desc *desc, const dcn_ex_options *opt,
+                                         const void *input, const void *weight, const void *offset,
+                                         const void *mask, const void *bias, void *output, void *saved,
+                                         size_t saved_bytes, void *workspace, size_t workspace_bytes,
+                                         void *stream);
+DCN_API int dcn_deform_conv2d_backward_ex(const dcn_conv_desc *desc, const dcn_ex_options *opt,
+                                          const void *grad_output, const void *input,
+                                          const void *weight, const void *offset, const void *mask,
+                                          const void *saved, size_t saved_bytes, void *grad_input,
+                                          void *grad_weight, void *grad_offset, void *grad_mask,
+                                          void *grad_bias, void *workspace, size_t workspace_bytes,
+                                          void *stream);
 
 /* ---------------------------------------------------------------------
  * Backward with a parameter-gradient callback, for overlapping the

@@ -503,56 +503,141 @@ int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc* d, const void* grad_
                        stream, params_ready, user_data);
 }
 
-// ---------------------------------------------------------------- DCNv2 head layout
-// offset_mask [B][OG*T*3][Ho][Wo]: offsets in channels [0, 2*OG*T), mask
+// ---------------------------------------------------------------- layouts and the DCNv2 head
+// dcn_ex_options: channels-last input / output and the DCNv2 head layout
+// (offset_mask [B][OG*T*3][Ho][Wo]: offsets in channels [0, 2*OG*T), mask
 // logits in [2*OG*T, 3*OG*T); the kernels read both in place and apply the
-// sigmoid.  Tensor-core path with 32-channel dgrad slabs only.
-static Geom head_geom(const dcn_conv_desc& d) {
+// sigmoid).  Anything but NCHW without the head needs the tensor-core path;
+// the head also needs 32-channel dgrad slabs.
+static bool plain_options(const dcn_ex_options* o) {
+  return !o || (o->input_layout == DCN_LAYOUT_NCHW && o->output_layout == DCN_LAYOUT_NCHW && !o->head);
+}
+
+static Geom ex_geom(const dcn_conv_desc& d, const dcn_ex_options* o) {
   Geom g = make_geom(d);
-  g.off_bs = 3LL * g.OG * g.T * g.HWo;
-  g.msk_bs = g.off_bs;
-  g.msk_logit = 1;
+  if (o && o->head) {
+    g.off_bs = 3LL * g.OG * g.T * g.HWo;
+    g.msk_bs = g.off_bs;
+    g.msk_logit = 1;
+  }
+  g.in_nhwc = o && o->input_layout == DCN_LAYOUT_NHWC;
+  g.out_nhwc = o && o->output_layout == DCN_LAYOUT_NHWC;
   return g;
 }
 
-int dcn_head_supported(const dcn_conv_desc* d) {
-  if (validate(d) != DCN_OK || !d->use_mask) return 0;
-  const Geom g = head_geom(*d);
-  return (tc_backward_supported(*d, g) && g.cpo % 32 == 0 && (long long)g.B * g.H * g.W * g.C < (1LL << 31))
-             ? 1
-             : 0;
+int dcn_ex_supported(const dcn_conv_desc* d, const dcn_ex_options* o, int backward) {
+  if (validate(d) != DCN_OK) return 0;
+  if (plain_options(o)) return 1;
+  if ((o->input_layout != DCN_LAYOUT_NCHW && o->input_layout != DCN_LAYOUT_NHWC) ||
+      (o->output_layout != DCN_LAYOUT_NCHW && o->output_layout != DCN_LAYOUT_NHWC) || (o->head != 0 && o->head != 1))
+    return 0;
+  const Geom g = ex_geom(*d, o);
+  if (o->head && (!d->use_mask || g.cpo % 32 != 0 || (long long)g.B * g.H * g.W * g.C >= (1LL << 31) ||
+                  !tc_backward_supported(*d, g)))
+    return 0;
+  return (backward ? tc_backward_supported(*d, g) : tc_forward_supported(*d, g)) ? 1 : 0;
 }
 
-static int head_check(const dcn_conv_desc* d, const char* fn) {
+int dcn_head_supported(const dcn_conv_desc* d) {
+  const dcn_ex_options o = {DCN_LAYOUT_NCHW, DCN_LAYOUT_NCHW, 1, 0};
+  return dcn_ex_supported(d, &o, 1);
+}
+
+static int ex_check(const dcn_conv_desc* d, const dcn_ex_options* o, int backward, const char* fn) {
   const int r = validate(d);
   if (r != DCN_OK) return r;
-  if (!dcn_head_supported(d))
+  if (!dcn_ex_supported(d, o, backward))
     return fail(DCN_ERR_UNSUPPORTED,
-                "%s: the DCNv2 head layout needs use_mask, fp16/bf16, per-group channels that the tensor-core "
-                "kernels take and offset groups of a multiple of 32 channels",
+                "%s: channels-last layouts and the DCNv2 head layout need fp16/bf16 with per-group channels that "
+                "the tensor-core kernels take (the head layout also needs use_mask and offset groups of a "
+                "multiple of 32 channels)",
                 fn);
   return DCN_OK;
 }
 
-int dcn_deform_conv2d_forward_head(const dcn_conv_desc* d, const void* input, const void* weight,
-                                   const void* offset_mask, const void* bias, void* output, void* saved,
-                                   size_t saved_bytes, void* workspace, size_t workspace_bytes, void* stream) {
-  int r = head_check(d, "deform_conv2d_forward_head");
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int dcn_deform_conv2d_forward_ex(const dcn_conv_desc* d, const dcn_ex_options* o, const void* input,
+                                 const void* weight, const void* offset, const void* mask, const void* bias,
+                                 void* output, void* saved, size_t saved_bytes, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (plain_options(o))
+    return forward_impl(d, input, weight, offset, mask, bias, output,
+                        dcn_saved_state_bytes(d) ? saved : nullptr, saved_bytes, workspace, workspace_bytes, stream);
+  int r = ex_check(d, o, 0, "deform_conv2d_forward_ex");
   if (r != DCN_OK) return r;
-  const Geom g = head_geom(*d);
+  const Geom g = ex_geom(*d, o);
   if (g.P == 0) return ok();
-  if (!input || !weight || !offset_mask || !output)
-    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (input, weight, offset_mask, output)");
+  if (!input || !weight || !offset || !output || (d->use_mask && !o->head && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (input, weight, offset, output%s)",
+                d->use_mask && !o->head ? ", mask" : "");
+  if ((g.in_nhwc && !aligned16(input)) || (g.out_nhwc && !aligned16(output)))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "channels-last input and output must be 16-byte aligned");
   const size_t need = tc_forward_workspace(*d, g);
   if (workspace_bytes < need || (need && !workspace))
     return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
   if (saved && saved_bytes < saved_layout(g).total)
     return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
                 saved_bytes);
-  const void* mask = static_cast<const char*>(offset_mask) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
-  cudaError_t e = tc_forward(*d, g, input, weight, offset_mask, mask, bias, output, workspace, saved,
+  if (o->head)
+    mask = static_cast<const char*>(offset) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
+  cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, saved,
                              (cudaStream_t)stream);
-  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward_head");
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward_ex");
+}
+
+int dcn_deform_conv2d_backward_ex(const dcn_conv_desc* d, const dcn_ex_options* o, const void* grad_output,
+                                  const void* input, const void* weight, const void* offset, const void* mask,
+                                  const void* saved, size_t saved_bytes, void* grad_input, void* grad_weight,
+                                  void* grad_offset, void* grad_mask, void* grad_bias, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (plain_options(o))
+    return dcn_deform_conv2d_backward_train(d, grad_output, input, weight, offset, mask, saved, saved_bytes,
+                                            grad_input, grad_weight, grad_offset, grad_mask, grad_bias, workspace,
+                                            workspace_bytes, stream);
+  int r = ex_check(d, o, 1, "deform_conv2d_backward_ex");
+  if (r != DCN_OK) return r;
+  const Geom g = ex_geom(*d, o);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (g.P == 0) {  // empty batch: parameter gradients are zero sums
+    cudaError_t e = cudaSuccess;
+    const size_t es = elem_size(d->dtype);
+    if (grad_weight) e = cudaMemsetAsync(grad_weight, 0, es * (size_t)g.Co * g.Cig * g.T, st);
+    if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, es * (size_t)g.Co, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_ex");
+  }
+  if (!grad_output || !input || !weight || !offset || (d->use_mask && !o->head && !mask))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (grad_output, input, weight, offset%s)",
+                d->use_mask && !o->head ? ", mask" : "");
+  if (g.in_nhwc && !aligned16(input))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "channels-last input must be 16-byte aligned");
+  const size_t need = tc_backward_workspace(*d, g);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+  if (saved && saved_bytes < saved_layout(g).total)
+    return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
+                saved_bytes);
+  if (o->head) {
+    mask = static_cast<const char*>(offset) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
+    grad_mask = nullptr;  // grad_offset holds the whole head gradient
+  }
+  if (!d->use_mask) grad_mask = nullptr;
+  cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset, mask, saved, grad_input, grad_weight,
+                              grad_offset, grad_mask, grad_bias, workspace, st, nullptr, nullptr);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_ex");
+}
+
+int dcn_deform_conv2d_forward_head(const dcn_conv_desc* d, const void* input, const void* weight,
+                                   const void* offset_mask, const void* bias, void* output, void* saved,
+                                   size_t saved_bytes, void* workspace, size_t workspace_bytes, void* stream) {
+  if (validate(d) != DCN_OK) return validate(d);
+  if (!dcn_head_supported(d))
+    return fail(DCN_ERR_UNSUPPORTED, "deform_conv2d_forward_head: the DCNv2 head layout needs use_mask, fp16/bf16, "
+                                     "per-group channels that the tensor-core kernels take and offset groups of a "
+                                     "multiple of 32 channels");
+  const dcn_ex_options o = {DCN_LAYOUT_NCHW, DCN_LAYOUT_NCHW, 1, 0};
+  return dcn_deform_conv2d_forward_ex(d, &o, input, weight, offset_mask, nullptr, bias, output, saved, saved_bytes,
+                                      workspace, workspace_bytes, stream);
 }
 
 int dcn_deform_conv2d_backward_head(const dcn_conv_desc* d, const void* grad_output, const void* input,
@@ -560,29 +645,15 @@ int dcn_deform_conv2d_backward_head(const dcn_conv_desc* d, const void* grad_out
                                     size_t saved_bytes, void* grad_input, void* grad_weight,
                                     void* grad_offset_mask, void* grad_bias, void* workspace,
                                     size_t workspace_bytes, void* stream) {
-  int r = head_check(d, "deform_conv2d_backward_head");
-  if (r != DCN_OK) return r;
-  const Geom g = head_geom(*d);
-  cudaStream_t st = (cudaStream_t)stream;
-  if (g.P == 0) {  // empty batch: parameter gradients are zero sums
-    cudaError_t e = cudaSuccess;
-    const size_t es = elem_size(d->dtype);
-    if (grad_weight) e = cudaMemsetAsync(grad_weight, 0, es * (size_t)g.Co * g.Cig * g.T, st);
-    if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, es * (size_t)g.Co, st);
-    return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_head");
-  }
-  if (!grad_output || !input || !weight || !offset_mask)
-    return fail(DCN_ERR_INVALID_ARGUMENT, "NULL tensor pointer (grad_output, input, weight, offset_mask)");
-  const size_t need = tc_backward_workspace(*d, g);
-  if (workspace_bytes < need || (need && !workspace))
-    return fail(DCN_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
-  if (saved && saved_bytes < saved_layout(g).total)
-    return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
-                saved_bytes);
-  const void* mask = static_cast<const char*>(offset_mask) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
-  cudaError_t e = tc_backward(*d, g, grad_output, input, weight, offset_mask, mask, saved, grad_input, grad_weight,
-                              grad_offset_mask, nullptr, grad_bias, workspace, st, nullptr, nullptr);
-  return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_head");
+  if (validate(d) != DCN_OK) return validate(d);
+  if (!dcn_head_supported(d))
+    return fail(DCN_ERR_UNSUPPORTED, "deform_conv2d_backward_head: the DCNv2 head layout needs use_mask, fp16/bf16, "
+                                     "per-group channels that the tensor-core kernels take and offset groups of a "
+                                     "multiple of 32 channels");
+  const dcn_ex_options o = {DCN_LAYOUT_NCHW, DCN_LAYOUT_NCHW, 1, 0};
+  return dcn_deform_conv2d_backward_ex(d, &o, grad_output, input, weight, offset_mask, nullptr, saved, saved_bytes,
+                                       grad_input, grad_weight, grad_offset_mask, nullptr, grad_bias, workspace,
+                                       workspace_bytes, stream);
 }
 
 int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void* grad_col,

@@ -52,6 +52,9 @@ struct Geom {
   // head output [B][OG*T*3][Ho][Wo] (offsets first, then mask logits).
   long long off_bs, msk_bs;
   int msk_logit;
+  // Memory formats: input / grad_input and output / grad_output are
+  // channels-last ([B][H][W][C]) instead of NCHW (tensor-core path only).
+  int in_nhwc, out_nhwc;
 };
 
 inline Geom make_geom(const dcn_conv_desc& d) {
@@ -72,6 +75,8 @@ inline Geom make_geom(const dcn_conv_desc& d) {
   g.off_bs = (long long)g.OG * 2 * g.T * g.HWo;
   g.msk_bs = (long long)g.OG * g.T * g.HWo;
   g.msk_logit = 0;
+  g.in_nhwc = 0;
+  g.out_nhwc = 0;
   return g;
 }
 

@@ -162,12 +162,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
         tmem_ld_wait();
         if (ovalid) {
           const int oc0 = grp * g.Cog + c0;
-          T* dst = out + ((long long)ob * g.Co + oc0) * g.HWo + op;
+          float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float v = __uint_as_float(acc[j]);
-            if (bias) v += to_f(bias[oc0 + j]);
-            dst[(long long)j * g.HWo] = from_f<T>(v);
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(acc[j]) + (bias ? to_f(bias[oc0 + j]) : 0.f);
+          if (g.out_nhwc) {  // channels-last output: the row's 16 channels are 32 contiguous bytes
+            uint4* dst = reinterpret_cast<uint4*>(out + opix * g.Co + oc0);
+            dst[0] = make_uint4(Vec<T>::pack(v[0], v[1]), Vec<T>::pack(v[2], v[3]), Vec<T>::pack(v[4], v[5]),
+                                Vec<T>::pack(v[6], v[7]));
+            dst[1] = make_uint4(Vec<T>::pack(v[8], v[9]), Vec<T>::pack(v[10], v[11]), Vec<T>::pack(v[12], v[13]),
+                                Vec<T>::pack(v[14], v[15]));
+          } else {
+            T* dst = out + ((long long)ob * g.Co + oc0) * g.HWo + op;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) dst[(long long)j * g.HWo] = from_f<T>(v[j]);
           }
         }
       }
@@ -373,11 +380,13 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
                                 const T* bias, T* out, void* workspace, void* saved, cudaStream_t st) {
   const FwdWs L = fwd_ws(g, sizeof(T));
   const SavedLayout SV = saved_layout(g);
-  T* xh = reinterpret_cast<T*>(saved ? static_cast<char*>(saved) + SV.xh
-                                     : static_cast<char*>(workspace) + L.xh);
+  // channels-last input: the gather reads it directly; else a channels-last copy
+  T* xh = g.in_nhwc ? const_cast<T*>(x)
+                    : reinterpret_cast<T*>(saved ? static_cast<char*>(saved) + SV.xh
+                                                 : static_cast<char*>(workspace) + L.xh);
   T* wsw = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.wsw);
   cudaError_t e;
-  {
+  if (!g.in_nhwc) {
     KernelScope ks("nchw_to_nhwc", st);
     const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
     if (layout::to_channels_last_vec_ok(x, xh, g.C, (long long)g.H * g.W))

@@ -1058,6 +1058,35 @@ wgrad_reduce_kernel(const float* __restrict__ gwp, T* __restrict__ gw, const flo
   }
 }
 
+// gb32[co] += sum over pixels of go[p][co] for a channels-last grad_output
+// [P][Co] (Co even, go 4-byte aligned).  A warp reads 64 channels (128 bytes)
+// of one pixel row; 8 warps take 8 rows at a time; blockIdx.y strides the rows.
+template <typename T>
+__global__ void __launch_bounds__(256) bias_rows_kernel(const T* __restrict__ go, float* __restrict__ gb32,
+                                                        long long P, int Co) {
+  __shared__ float red[8][64];
+  const int cp = threadIdx.x & 31, r0 = threadIdx.x >> 5;
+  const int c = blockIdx.x * 64 + 2 * cp;
+  float s0 = 0.f, s1 = 0.f;
+  if (c < Co) {
+    for (long long p = (long long)blockIdx.y * 8 + r0; p < P; p += (long long)gridDim.y * 8) {
+      const float2 f = Vec<T>::unpack(*reinterpret_cast<const uint32_t*>(go + p * Co + c));
+      s0 += f.x;
+      s1 += f.y;
+    }
+  }
+  red[r0][2 * cp] = s0;
+  red[r0][2 * cp + 1] = s1;
+  __syncthreads();
+  const int cc = blockIdx.x * 64 + threadIdx.x;
+  if (threadIdx.x < 64 && cc < Co) {
+    float t = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) t += red[r][threadIdx.x];
+    atomicAdd(gb32 + cc, t);
+  }
+}
+
 // ================================================================ host
 // Work split of the weight-gradient GEMM: CTAs own nkg K chunks (TMEM holds
 // mh * nkg * 64 fp32 columns <= 512) of one group and a contiguous range of
@@ -1123,10 +1152,15 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   const BwdWs L = bwd_ws(g, sizeof(T));
   char* ws = static_cast<char*>(workspace);
   const SavedLayout SV = saved_layout(g);
-  T* xh = saved ? reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.xh)
-                : reinterpret_cast<T*>(ws + L.xh);
+  // channels-last input: read in place; else the forward's copy or a new one
+  T* xh = g.in_nhwc ? const_cast<T*>(x)
+                    : saved ? reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.xh)
+                            : reinterpret_cast<T*>(ws + L.xh);
   const void* cols = saved ? static_cast<const char*>(saved) + SV.cols : nullptr;
-  T* got = reinterpret_cast<T*>(ws + L.got);
+  // channels-last grad_output is already the pixel-major [P][Co] operand (the
+  // tensor map wants a 16-byte aligned base: otherwise it is copied once)
+  const bool go_direct = g.out_nhwc && (reinterpret_cast<uintptr_t>(go) & 15) == 0;
+  T* got = go_direct ? const_cast<T*>(go) : reinterpret_cast<T*>(ws + L.got);
   T* wdt = reinterpret_cast<T*>(ws + L.wdt);
   float* gi32 = reinterpret_cast<float*>(ws + L.gi32);
   float* goff32 = reinterpret_cast<float*>(ws + L.goff32);
@@ -1142,7 +1176,15 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   cudaError_t e;
 
   if ((e = cudaMemsetAsync(ws + L.acc, 0, L.acc_bytes, st)) != cudaSuccess) return e;
-  {
+  if (g.out_nhwc) {
+    if (!go_direct && (e = cudaMemcpyAsync(got, go, sizeof(T) * (size_t)g.P * g.Co, cudaMemcpyDeviceToDevice,
+                                           st)) != cudaSuccess)
+      return e;
+    if (gb) {
+      KernelScope ks("bias_rows", st);
+      bias_rows_kernel<T><<<dim3((unsigned)((g.Co + 63) / 64), 296), 256, 0, st>>>(got, gb32, g.P, g.Co);
+    }
+  } else {
     KernelScope ks("go_transpose_bias", st);
     const dim3 grid = layout::tile_grid(g.Co, g.HWo, g.B);
     if (!layout::to_channels_last_vec_ok(go, got, g.Co, g.HWo))
@@ -1153,7 +1195,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       layout::to_channels_last16_kernel<T, false><<<grid, layout::LAYOUT_THREADS, 0, st>>>(go, got, nullptr, g.Co, g.HWo);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (!saved) {  // channels-last input copy, unless the forward left one
+  if (!saved && !g.in_nhwc) {  // channels-last input copy, unless the forward left one or the input is one
     KernelScope ks("nchw_to_nhwc", st);
     const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
     if (layout::to_channels_last_vec_ok(x, xh, g.C, (long long)g.H * g.W))
@@ -1272,7 +1314,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   // collective's blocks would take SMs from them.
   if (ready) ready(user);
   // ---- finalize
-  if (gin) {
+  if (gin && !g.in_nhwc) {
     KernelScope ks("grad_input_to_nchw", st);
     const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
     if (layout::from_channels_last_vec_ok(gi32, gin, g.C, (long long)g.H * g.W))
@@ -1282,11 +1324,12 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  {  // offset / mask gradients: fp32 -> T in one launch
+  {  // offset / mask (and channels-last input) gradients: fp32 -> T in one launch
     ConvertJobs jobs{};
     auto add = [&](const float* src, void* dst, long long n) {
       if (dst && n > 0) { jobs.src[jobs.n] = src; jobs.dst[jobs.n] = dst; jobs.count[jobs.n] = n; ++jobs.n; }
     };
+    if (gin && g.in_nhwc) add(gi32, gin, (long long)g.B * g.H * g.W * g.C);  // channels-last: no transpose
     if (g.msk_logit) {  // DCNv2 head layout: goff is the whole [B][3*OG*T][HWo] gradient
       add(goff32, goff, (long long)g.B * g.off_bs);
     } else {

@@ -96,6 +96,29 @@ std::pair<int64_t, int64_t> out_size(const dcn_conv_desc& d) {
   return {oh, ow};
 }
 
+// PyTorch's channels_last memory format (and not also plain contiguous, as
+// when C == 1 or H*W == 1).
+bool channels_last(const at::Tensor& t) {
+  return t.dim() == 4 && !t.is_contiguous() && t.is_contiguous(at::MemoryFormat::ChannelsLast);
+}
+
+// Dense tensor in the requested format, 16-byte aligned when channels-last.
+at::Tensor in_layout(const at::Tensor& t, bool nhwc) {
+  if (!nhwc) return t.contiguous();
+  at::Tensor r = t.contiguous(at::MemoryFormat::ChannelsLast);
+  if ((reinterpret_cast<uintptr_t>(r.data_ptr()) & 15) != 0) r = r.clone(at::MemoryFormat::ChannelsLast);
+  return r;
+}
+
+dcn_ex_options ex_options(bool in_nhwc, bool out_nhwc, bool head) {
+  dcn_ex_options o;
+  o.input_layout = in_nhwc ? DCN_LAYOUT_NHWC : DCN_LAYOUT_NCHW;
+  o.output_layout = out_nhwc ? DCN_LAYOUT_NHWC : DCN_LAYOUT_NCHW;
+  o.head = head ? 1 : 0;
+  o.reserved = 0;
+  return o;
+}
+
 }  // namespace
 
 // Reference: deform_conv2d_forward_mps, deform_conv2d_mps.mm:603-800.
@@ -172,6 +195,53 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_train(
                                                has_bias ? b.data_ptr() : nullptr, out.data_ptr(),
                                                sbytes ? saved.data_ptr() : nullptr, sbytes,
                                                ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+  return {out, saved};
+}
+
+// Forward of the autograd path: like forward_train, and a channels_last input
+// gives a channels_last output (read and written in place by the tensor-core
+// kernels; other problems run on NCHW copies and convert the output back).
+// keep_saved: also return the state the backward reuses (else an empty tensor).
+std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_ex(
+    const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
+    const at::Tensor& bias, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+    int64_t dilation_h, int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask,
+    bool keep_saved) {
+  TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
+  check_cuda(weight, "weight", input);
+  check_cuda(offset, "offset", input);
+  const bool has_mask = use_mask && mask.numel() > 0;
+  if (has_mask) check_cuda(mask, "mask", input);
+  const bool has_bias = bias.defined() && bias.numel() > 0;
+  if (has_bias) check_cuda(bias, "bias", input);
+  TORCH_CHECK(weight.dim() == 4, "weight must be 4-D");
+  c10::cuda::CUDAGuard guard(input.device());
+  dcn_conv_desc d = make_desc(input, weight.size(0), weight.size(2), weight.size(3), stride_h,
+                              stride_w, pad_h, pad_w, dilation_h, dilation_w, n_weight_grps,
+                              n_offset_grps, has_mask);
+  TORCH_CHECK(weight.size(1) * n_weight_grps == input.size(1), "weight in_channels (",
+              weight.size(1), ") x n_weight_grps (", n_weight_grps, ") must equal in_channels (",
+              input.size(1), ")");
+  auto [oh, ow] = out_size(d);
+  check_offset_mask(d, offset, mask, oh, ow);
+  if (has_bias) TORCH_CHECK(bias.numel() == weight.size(0), "bias must have out_channels elements");
+  const bool want_nhwc = channels_last(input);
+  dcn_ex_options o = ex_options(want_nhwc, want_nhwc, false);
+  const bool nhwc = want_nhwc && dcn_ex_supported(&d, &o, 0);
+  if (!nhwc) o = ex_options(false, false, false);
+  auto x = in_layout(input, nhwc), w = weight.contiguous(), off = offset.contiguous();
+  auto m = has_mask ? mask.contiguous() : at::Tensor();
+  auto b = has_bias ? bias.contiguous() : at::Tensor();
+  auto out = at::empty({d.batch, d.out_channels, oh, ow},
+                       input.options().memory_format(nhwc ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous));
+  const size_t sbytes = keep_saved ? dcn_saved_state_bytes(&d) : 0;
+  auto saved = at::empty({(int64_t)sbytes}, input.options().dtype(at::kByte));
+  auto ws = workspace(dcn_forward_workspace_size(&d), input);
+  check_status(dcn_deform_conv2d_forward_ex(&d, &o, x.data_ptr(), w.data_ptr(), off.data_ptr(),
+                                            has_mask ? m.data_ptr() : nullptr, has_bias ? b.data_ptr() : nullptr,
+                                            out.data_ptr(), sbytes ? saved.data_ptr() : nullptr, sbytes,
+                                            ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+  if (want_nhwc && !nhwc) out = out.contiguous(at::MemoryFormat::ChannelsLast);
   return {out, saved};
 }
 
@@ -289,7 +359,15 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
                   grad_output.size(3) == ow,
               "grad_output has shape ", grad_output.sizes(), ", expected (", d.batch, ", ",
               d.out_channels, ", ", oh, ", ", ow, ")");
-  auto go = grad_output.contiguous(), x = input.contiguous(), w = weight.contiguous(),
+  // channels_last input / grad_output are used in place when the tensor-core
+  // kernels take the problem (grad_input then comes back channels_last too)
+  bool in_nhwc = channels_last(input), out_nhwc = channels_last(grad_output);
+  dcn_ex_options o = ex_options(in_nhwc, out_nhwc, false);
+  if ((in_nhwc || out_nhwc) && !dcn_ex_supported(&d, &o, 1)) {
+    in_nhwc = out_nhwc = false;
+    o = ex_options(false, false, false);
+  }
+  auto go = in_layout(grad_output, out_nhwc), x = in_layout(input, in_nhwc), w = weight.contiguous(),
        off = offset.contiguous();
   auto m = has_mask ? mask.contiguous() : at::Tensor();
   at::Tensor gin, gw, goff, gm, gb;
@@ -307,11 +385,14 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
                     saved.is_contiguous(),
                 "saved state must be a contiguous uint8 tensor on the input's device");
   }
-  if (!params_ready.has_value() || params_ready->is_none()) {
-    check_status(dcn_deform_conv2d_backward_train(
-        &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
+  const bool hook = params_ready.has_value() && !params_ready->is_none();
+  if (!hook || in_nhwc || out_nhwc) {
+    check_status(dcn_deform_conv2d_backward_ex(
+        &d, &o, go.data_ptr(), x.data_ptr(), w.data_ptr(), off.data_ptr(), has_mask ? m.data_ptr() : nullptr,
         has_saved ? saved.data_ptr() : nullptr, has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw),
         ptr(goff), ptr(gm), ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
+    if (hook)  // channels-last layouts have no callback entry point: the hook runs after the whole backward
+      (*params_ready)(gw.defined() ? py::cast(gw) : py::none(), gb.defined() ? py::cast(gb) : py::none());
     return {gin, gw, goff, gm, gb};
   }
   // params_ready(grad_weight, grad_bias) runs inside the library call once
@@ -384,16 +465,22 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_head(
                               n_weight_grps, n_offset_grps);
   if (has_bias) TORCH_CHECK(bias.numel() == weight.size(0), "bias must have out_channels elements");
   auto [oh, ow] = out_size(d);
-  auto x = input.contiguous(), w = weight.contiguous(), om = offset_mask.contiguous();
+  const bool want_nhwc = channels_last(input);
+  dcn_ex_options o = ex_options(want_nhwc, want_nhwc, true);
+  const bool nhwc = want_nhwc && dcn_ex_supported(&d, &o, 0);
+  if (!nhwc) o = ex_options(false, false, true);
+  auto x = in_layout(input, nhwc), w = weight.contiguous(), om = offset_mask.contiguous();
   auto b = has_bias ? bias.contiguous() : at::Tensor();
-  auto out = at::empty({d.batch, d.out_channels, oh, ow}, input.options());
+  auto out = at::empty({d.batch, d.out_channels, oh, ow},
+                       input.options().memory_format(nhwc ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous));
   const size_t sbytes = keep_saved ? dcn_saved_state_bytes(&d) : 0;
   auto saved = at::empty({(int64_t)sbytes}, input.options().dtype(at::kByte));
   auto ws = workspace(dcn_forward_workspace_size(&d), input);
-  check_status(dcn_deform_conv2d_forward_head(&d, x.data_ptr(), w.data_ptr(), om.data_ptr(),
-                                              has_bias ? b.data_ptr() : nullptr, out.data_ptr(),
-                                              sbytes ? saved.data_ptr() : nullptr, sbytes, ws.data_ptr(),
-                                              (size_t)ws.numel(), stream_of(input)));
+  check_status(dcn_deform_conv2d_forward_ex(&d, &o, x.data_ptr(), w.data_ptr(), om.data_ptr(), nullptr,
+                                            has_bias ? b.data_ptr() : nullptr, out.data_ptr(),
+                                            sbytes ? saved.data_ptr() : nullptr, sbytes, ws.data_ptr(),
+                                            (size_t)ws.numel(), stream_of(input)));
+  if (want_nhwc && !nhwc) out = out.contiguous(at::MemoryFormat::ChannelsLast);
   return {out, saved};
 }
 
@@ -417,7 +504,14 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_conv2d_backwar
                   grad_output.size(2) == oh && grad_output.size(3) == ow,
               "grad_output has shape ", grad_output.sizes(), ", expected (", d.batch, ", ", d.out_channels, ", ", oh,
               ", ", ow, ")");
-  auto go = grad_output.contiguous(), x = input.contiguous(), w = weight.contiguous(), om = offset_mask.contiguous();
+  bool in_nhwc = channels_last(input), out_nhwc = channels_last(grad_output);
+  dcn_ex_options o = ex_options(in_nhwc, out_nhwc, true);
+  if ((in_nhwc || out_nhwc) && !dcn_ex_supported(&d, &o, 1)) {
+    in_nhwc = out_nhwc = false;
+    o = ex_options(false, false, true);
+  }
+  auto go = in_layout(grad_output, out_nhwc), x = in_layout(input, in_nhwc), w = weight.contiguous(),
+       om = offset_mask.contiguous();
   at::Tensor gin, gw, gom, gb;
   if (output_mask[0]) gin = at::empty_like(x);
   if (output_mask[1]) gw = at::empty_like(w);
@@ -431,10 +525,10 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_conv2d_backwar
     TORCH_CHECK(saved.is_cuda() && saved.device() == input.device() && saved.scalar_type() == at::kByte &&
                     saved.is_contiguous(),
                 "saved state must be a contiguous uint8 tensor on the input's device");
-  check_status(dcn_deform_conv2d_backward_head(
-      &d, go.data_ptr(), x.data_ptr(), w.data_ptr(), om.data_ptr(), has_saved ? saved.data_ptr() : nullptr,
-      has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw), ptr(gom), ptr(gb), ws.data_ptr(),
-      (size_t)ws.numel(), stream_of(input)));
+  check_status(dcn_deform_conv2d_backward_ex(
+      &d, &o, go.data_ptr(), x.data_ptr(), w.data_ptr(), om.data_ptr(), nullptr,
+      has_saved ? saved.data_ptr() : nullptr, has_saved ? (size_t)saved.numel() : 0, ptr(gin), ptr(gw), ptr(gom),
+      nullptr, ptr(gb), ws.data_ptr(), (size_t)ws.numel(), stream_of(input)));
   return {gin, gw, gom, gb};
 }
 
@@ -472,6 +566,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_weight_grps"), py::arg("n_offset_grps"), py::arg("use_mask"),
         py::arg("output_mask") = std::vector<bool>{true, true, true, true, true},
         py::arg("saved") = py::none(), py::arg("params_ready") = py::none());
+  m.def("deform_conv2d_forward_ex", &deform_conv2d_forward_ex,
+        "Forward of the autograd path (channels_last in, channels_last out): (output, saved)");
   m.def("deform_conv2d_forward_train", &deform_conv2d_forward_train,
         "Forward that also returns the device state its backward reuses: (output, saved)");
   m.def("uses_tensor_cores", &uses_tensor_cores, "True when the tcgen05 kernels run this problem");

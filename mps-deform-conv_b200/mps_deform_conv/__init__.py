@@ -234,20 +234,16 @@ class _DeformConv2dFunction(torch.autograd.Function):
         bias_t = bias if bias is not None else torch.empty(0, device=input.device, dtype=input.dtype)
         mask_t = mask if mask is not None else torch.empty(0, device=input.device, dtype=input.dtype)
 
-        if _training_cache and ctx.needs_input_grad[2]:
-            output, saved = lib.deform_conv2d_forward_train(
-                input, weight, offset, mask_t, bias_t,
-                stride_h, stride_w, pad_h, pad_w,
-                dilation_h, dilation_w,
-                n_weight_grps, n_offset_grps, use_mask,
-            )
-        else:
-            output = lib.deform_conv2d_forward(
-                input, weight, offset, mask_t, bias_t,
-                stride_h, stride_w, pad_h, pad_w,
-                dilation_h, dilation_w,
-                n_weight_grps, n_offset_grps, use_mask,
-            )
+        # a channels_last input gives a channels_last output (read and written in
+        # place by the tensor-core kernels)
+        keep = bool(_training_cache and ctx.needs_input_grad[2])
+        output, saved = lib.deform_conv2d_forward_ex(
+            input, weight, offset, mask_t, bias_t,
+            stride_h, stride_w, pad_h, pad_w,
+            dilation_h, dilation_w,
+            n_weight_grps, n_offset_grps, use_mask, keep,
+        )
+        if saved.numel() == 0:
             saved = None
 
         ctx.save_for_backward(input, offset, weight, mask_t if use_mask else None, saved)

@@ -38,6 +38,17 @@ class DcnConvDesc(ctypes.Structure):
 
 # name -> (restype, argtypes); the exported surface of include/dcn_b200.h
 _D = ctypes.POINTER(DcnConvDesc)
+DCN_LAYOUT_NCHW = 0
+DCN_LAYOUT_NHWC = 1
+
+
+class DcnExOptions(ctypes.Structure):
+    """dcn_ex_options of include/dcn_b200.h."""
+    _fields_ = [("input_layout", ctypes.c_int32), ("output_layout", ctypes.c_int32), ("head", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
+_O = ctypes.POINTER(DcnExOptions)
 # void (*dcn_params_ready_fn)(void* user_data)
 PARAMS_READY_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 _V = ctypes.c_void_p
@@ -67,6 +78,10 @@ SIGNATURES = {
     "dcn_deform_conv2d_backward_overlap": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V,
                                                           _V, _SZ, _V, PARAMS_READY_FN, _V]),
     "dcn_head_supported": (ctypes.c_int, [_D]),
+    "dcn_ex_supported": (ctypes.c_int, [_D, _O, ctypes.c_int]),
+    "dcn_deform_conv2d_forward_ex": (ctypes.c_int, [_D, _O, _V, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
+    "dcn_deform_conv2d_backward_ex": (ctypes.c_int, [_D, _O, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V, _V,
+                                                     _SZ, _V]),
     "dcn_deform_conv2d_forward_head": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
     "dcn_deform_conv2d_backward_head": (ctypes.c_int, [_D, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V, _SZ,
                                                        _V]),
