@@ -523,9 +523,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
     //      computes the sample's corners into its table row;
     //  (2) 8 lanes per pixel, 4 channels per lane, 4 pixels per instruction:
     //      corner loads and red.global.add.v4.f32 scatters cover whole lines;
-    //      the offset/mask partial sums are reduced over the pixel's 8 lanes
-    //      by shuffles and taken by the row owner, which adds them to global
-    //      memory once per (pixel, offset group, K chunk).
+    //      each lane leaves its offset/mask partial sums in the slab chunk it
+    //      has just consumed, and the row owner sums its row's 8 chunks and
+    //      adds the result to global memory once per (pixel, offset group,
+    //      K chunk).
     const T* xh = static_cast<const T*>(a.xh);
     const T* off = static_cast<const T*>(a.off);
     const T* msk = static_cast<const T*>(a.msk);
@@ -645,22 +646,19 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
             const float wk = w[k] * m;
             if (wk != 0.f) red_v4(a.gi32 + eo[k], wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
           }
+          // the lane's partial sums replace the slab chunk it alone has read
+          *reinterpret_cast<float4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2)) = make_float4(pgy, pgx, pgm, 0.f);
+        }
+        __syncwarp();
+        // ---- row owner: sum the 8 lanes' partials of its row
+        {
+          const float* srow = ws->slab[lane];
 #pragma unroll
-          for (int sh = 1; sh < 8; sh <<= 1) {
-            pgy += __shfl_xor_sync(0xffffffffu, pgy, sh);
-            pgx += __shfl_xor_sync(0xffffffffu, pgx, sh);
-            pgm += __shfl_xor_sync(0xffffffffu, pgm, sh);
-          }
-          // rows it*4 .. it*4+3 are owned by lanes it*4 .. it*4+3; their sums
-          // sit in lanes 0, 8, 16, 24
-          const int src = (lane & 3) * 8;
-          const float sy = __shfl_sync(0xffffffffu, pgy, src);
-          const float sx = __shfl_sync(0xffffffffu, pgx, src);
-          const float sm = __shfl_sync(0xffffffffu, pgm, src);
-          if ((lane >> 2) == it) {
-            run_gy += sy;
-            run_gx += sx;
-            run_gm += sm;
+          for (int k = 0; k < 8; ++k) {
+            const float4 pv = *reinterpret_cast<const float4*>(srow + ((k ^ (lane & 7)) << 2));
+            run_gy += pv.x;
+            run_gx += pv.y;
+            run_gm += pv.z;
           }
         }
         __syncwarp();
