@@ -445,6 +445,15 @@ struct DgWarpSmem32 {
   uint32_t tab[32][12];
 };
 
+// 64-channel-slab variant (offset groups of a multiple of 64 channels, so a
+// whole K chunk has one sample per pixel): the chunk's gcol row as 16-bit
+// pairs (the precision of the reference's own 16-bit GEMM output), 16-byte
+// chunk k of row r at chunk k ^ (r & 7), and the same per-row sample table.
+struct DgWarpSmem64 {
+  uint32_t slab[32][32];
+  uint32_t tab[32][12];
+};
+
 // Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
 // streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each;
 // then the epilogue warps' scratch.
@@ -457,7 +466,9 @@ __host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages, int sw) {
   L.b = (uint32_t)kb * A_STAGE_BYTES;
   L.b_stage = 8192u;
   L.epi = L.b + b_stages * L.b_stage;
-  L.bar = L.epi + D_EPI_WARPS * (uint32_t)(sw == 32 ? sizeof(DgWarpSmem32) : sizeof(DgWarpSmem));
+  L.bar = L.epi + D_EPI_WARPS * (uint32_t)(sw == 64   ? sizeof(DgWarpSmem64)
+                                            : sw == 32 ? sizeof(DgWarpSmem32)
+                                                       : sizeof(DgWarpSmem));
   L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
   return L;
 }
@@ -467,11 +478,12 @@ __device__ __forceinline__ void red_v4(float* p, float a, float b, float c, floa
                : "memory");
 }
 
-// SW = channels per epilogue slab: 32 when the offset groups are a multiple
-// of 32 channels and B*H*W*C < 2^31 (8 lanes x 4 channels per pixel: each
-// corner's 32 fp32 gradients are one 128-byte line, half the lines per byte
-// of SW = 16; 32-bit element offsets), else 16 (4 lanes x 4 channels, up to
-// 2 offset groups per slab).
+// SW = channels per epilogue pass: 64 when the offset groups are a multiple
+// of 64 channels and B*H*W*C < 2^31 (one pass per K chunk, gcol held as
+// 16-bit pairs, 16-byte corner loads); 32 when they are a multiple of 32
+// channels (8 lanes x 4 channels per pixel: each corner's 32 fp32 gradients
+// are one 128-byte line, half the lines per byte of SW = 16; 32-bit element
+// offsets); else 16 (4 lanes x 4 channels, up to 2 offset groups per slab).
 template <typename T, int SW>
 __global__ void __launch_bounds__(D_NTHREADS, 1)
 dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
@@ -515,7 +527,161 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < D_EPI_WARPS && SW == 32) {
+  if (warp < D_EPI_WARPS && SW == 64) {
+    // -------------------------------------------- epilogue, one 64-channel pass per K chunk
+    //  (1) row owner (lane = TMEM row = pixel): its 64 gcol values to the
+    //      slab as 16-bit pairs (the TMEM buffer is then free for the next
+    //      MMA) and the sample of the chunk's offset group into the table;
+    //  (2) 8 lanes per pixel, 4 pixels per step: each lane loads 8
+    //      consecutive channels of the 4 corners (16 bytes: one instruction
+    //      covers 4 whole 128-byte lines) for the offset/mask dot products,
+    //      and scatters channels 4j..4j+3 and 32+4j..32+4j+3 with two
+    //      red.global.add.v4.f32 per corner (again whole lines); its partial
+    //      sums go to the slab chunk it has consumed, and the row owner adds
+    //      its row's 8 chunks to global memory once per (pixel, K chunk).
+    const T* xh = static_cast<const T*>(a.xh);
+    const T* off = static_cast<const T*>(a.off);
+    const T* msk = static_cast<const T*>(a.msk);
+    const int e = warp >> 2, q = warp & 3;
+    DgWarpSmem64* ws = reinterpret_cast<DgWarpSmem64*>(smem + L.epi) + warp;
+    const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
+    const int j8 = lane & 7, rsub = lane >> 3;
+    bool ok = true;
+    for (int i = e; i < nkc_cta; i += D_NBUF) {
+      const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
+      ok = __all_sync(0xffffffffu, ready);
+      if (!ok) break;
+      tc_fence_after();
+      KWalk kw;
+      kw.start(g, kc_lo + i);
+      const int cbase = grp * g.Cig + kw.cc * BK;
+      // ---- phase 1: row owner
+      {
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64);
+        uint32_t* srow = ws->slab[lane];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // channels 32h .. 32h+31 = chunks 4h .. 4h+3
+          uint32_t a0[16], a1[16];
+          tmem_ld16(taddr + h * 32, a0);
+          tmem_ld16(taddr + h * 32 + 16, a1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            *reinterpret_cast<uint4*>(srow + (((4 * h + k) ^ (lane & 7)) << 2)) = make_uint4(
+                Vec<T>::pack(__uint_as_float(a0[8 * k]), __uint_as_float(a0[8 * k + 1])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 2]), __uint_as_float(a0[8 * k + 3])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 4]), __uint_as_float(a0[8 * k + 5])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 6]), __uint_as_float(a0[8 * k + 7])));
+            *reinterpret_cast<uint4*>(srow + (((4 * h + 2 + k) ^ (lane & 7)) << 2)) = make_uint4(
+                Vec<T>::pack(__uint_as_float(a1[8 * k]), __uint_as_float(a1[8 * k + 1])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 2]), __uint_as_float(a1[8 * k + 3])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 4]), __uint_as_float(a1[8 * k + 5])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 6]), __uint_as_float(a1[8 * k + 7])));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(d_empty(e));  // TMEM buffer read completely
+      }
+      const int o = cbase / g.cpo;  // one offset group per chunk
+      float tab_m;
+      {
+        const RawSample<T> raw = load_raw(g, off, msk, pc, o, kw.t);
+        const SamplePos sp = sample_pos(pc.y0 + kw.ti * g.dh, pc.x0 + kw.tj * g.dw, to_f(raw.dy), to_f(raw.dx));
+        const Corners cs = corners_of(sp, g.H, g.W);
+        const CoordCorners c4 = coord_corners_of(sp, g.H, g.W);
+        uint32_t cvb = 0;
+        int cidx[4];
+        float cw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool v = pc.valid && c4.v[k];
+          cvb |= (v ? 1u : 0u) << k;
+          cidx[k] = v ? (int)((pc.img + c4.idx[k]) * g.C) : 0;  // element offset, B*H*W*C < 2^31
+          cw[k] = pc.valid ? cs.w[k] : 0.f;
+        }
+        tab_m = pc.valid ? mask_of(g, to_f(raw.m)) : 0.f;
+        uint32_t* trow = ws->tab[lane];
+        *reinterpret_cast<uint4*>(trow) = make_uint4(cidx[0], cidx[1], cidx[2], cidx[3]);
+        *reinterpret_cast<uint4*>(trow + 4) = make_uint4(__float_as_uint(cw[0]), __float_as_uint(cw[1]),
+                                                         __float_as_uint(cw[2]), __float_as_uint(cw[3]));
+        *reinterpret_cast<uint4*>(trow + 8) =
+            make_uint4(__float_as_uint(c4.fy), __float_as_uint(c4.fx), __float_as_uint(tab_m), cvb);
+      }
+      __syncwarp();
+      // ---- phase 2: 8 lanes per pixel, 4 pixels per step
+      const uint32_t cl = (uint32_t)(cbase + j8 * 8);                 // dot-product channels
+      const uint32_t cr0 = (uint32_t)(cbase + j8 * 4), cr1 = cr0 + 32;  // scattered channels
+#pragma unroll 1
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + rsub;
+        const uint32_t* tr = ws->tab[rr];
+        const uint4 tb = *reinterpret_cast<const uint4*>(tr);
+        const uint4 tw = *reinterpret_cast<const uint4*>(tr + 4);
+        const uint4 tx = *reinterpret_cast<const uint4*>(tr + 8);
+        uint32_t* srow = ws->slab[rr];
+        const int sw7 = rr & 7;
+        const uint4 gd = *reinterpret_cast<const uint4*>(srow + ((j8 ^ sw7) << 2));
+        const uint2 gr0 = *reinterpret_cast<const uint2*>(srow + (((j8 >> 1) ^ sw7) << 2) + (j8 & 1) * 2);
+        const uint2 gr1 = *reinterpret_cast<const uint2*>(srow + (((4 + (j8 >> 1)) ^ sw7) << 2) + (j8 & 1) * 2);
+        const uint32_t cof[4] = {tb.x, tb.y, tb.z, tb.w};
+        const float w[4] = {__uint_as_float(tw.x), __uint_as_float(tw.y), __uint_as_float(tw.z),
+                            __uint_as_float(tw.w)};
+        const float fy = __uint_as_float(tx.x), fx = __uint_as_float(tx.y), m = __uint_as_float(tx.z);
+        const uint32_t cv = tx.w;
+        uint4 xv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint4*>(xh + (cof[k] + cl))) : make_uint4(0, 0, 0, 0);
+        const float2 g01 = Vec<T>::unpack(gd.x), g23 = Vec<T>::unpack(gd.y), g45 = Vec<T>::unpack(gd.z),
+                     g67 = Vec<T>::unpack(gd.w);
+        float d[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x01 = Vec<T>::unpack(xv[k].x), x23 = Vec<T>::unpack(xv[k].y), x45 = Vec<T>::unpack(xv[k].z),
+                       x67 = Vec<T>::unpack(xv[k].w);
+          d[k] = g01.x * x01.x + g01.y * x01.y + g23.x * x23.x + g23.y * x23.y + g45.x * x45.x + g45.y * x45.y +
+                 g67.x * x67.x + g67.y * x67.y;
+        }
+        const float pgm = w[0] * d[0] + w[1] * d[1] + w[2] * d[2] + w[3] * d[3];
+        const float pgy = m * (fx * (d[3] - d[1]) + (1.f - fx) * (d[2] - d[0]));
+        const float pgx = m * (fy * (d[3] - d[2]) + (1.f - fy) * (d[1] - d[0]));
+        const float2 r01 = Vec<T>::unpack(gr0.x), r23 = Vec<T>::unpack(gr0.y);
+        const float2 r45 = Vec<T>::unpack(gr1.x), r67 = Vec<T>::unpack(gr1.y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float wk = w[k] * m;
+          if (wk != 0.f) {
+            red_v4(a.gi32 + (cof[k] + cr0), wk * r01.x, wk * r01.y, wk * r23.x, wk * r23.y);
+            red_v4(a.gi32 + (cof[k] + cr1), wk * r45.x, wk * r45.y, wk * r67.x, wk * r67.y);
+          }
+        }
+        __syncwarp();  // every lane has read this step's rows: the consumed chunks take the partial sums
+        *reinterpret_cast<float4*>(srow + ((j8 ^ sw7) << 2)) = make_float4(pgy, pgx, pgm, 0.f);
+      }
+      __syncwarp();
+      // ---- row owner: sum the 8 lanes' partials of its row, once per chunk
+      {
+        const uint32_t* srow = ws->slab[lane];
+        float gy = 0.f, gx = 0.f, gm = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 pv = *reinterpret_cast<const float4*>(srow + ((k ^ (lane & 7)) << 2));
+          gy += pv.x;
+          gx += pv.y;
+          gm += pv.z;
+        }
+        if (pc.valid) {
+          const long long ob = (long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          atomicAdd(a.goff32 + ob, gy);
+          atomicAdd(a.goff32 + ob + g.HWo, gx);
+          if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
+            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + pc.p,
+                      g.msk_logit ? gm * tab_m * (1.f - tab_m) : gm);
+        }
+      }
+      __syncwarp();  // the next chunk's phase 1 rewrites the rows
+    }
+  } else if (warp < D_EPI_WARPS && SW == 32) {
     // -------------------------------------------- epilogue, 32-channel slabs
     // Per slab of a gcol tile (one offset group):
     //  (1) row owner (lane = TMEM row = pixel): reads its 32 gcol values from
@@ -1284,12 +1450,13 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.b_stages = 4;
     // epilogue slab width (see the kernel); the 32-channel variant addresses
     // the input and grad_input with 32-bit element offsets
-    const int sw = (g.cpo % 32 == 0 && (long long)g.B * g.H * g.W * g.C < (1LL << 31)) ? 32 : 16;
+    const bool small_index = (long long)g.B * g.H * g.W * g.C < (1LL << 31);
+    const int sw = (g.cpo % 64 == 0 && small_index) ? 64 : (g.cpo % 32 == 0 && small_index) ? 32 : 16;
     while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) --a.b_stages;
     if (dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
     a.idesc = idesc_f16(BM, 64, bf16);
     const int smem = (int)dgrad_smem(KB, a.b_stages, sw).total + 1024;
-    auto kern = sw == 32 ? dcn_dgrad_tc_kernel<T, 32> : dcn_dgrad_tc_kernel<T, 16>;
+    auto kern = sw == 64 ? dcn_dgrad_tc_kernel<T, 64> : sw == 32 ? dcn_dgrad_tc_kernel<T, 32> : dcn_dgrad_tc_kernel<T, 16>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
       return e;
     // split the K chunks of a tile over ksplit CTAs when that fills the last

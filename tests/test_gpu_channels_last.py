@@ -5,8 +5,8 @@ a channels_last output, take a channels_last grad_output as the pixel-major
 GEMM operand and return grad_input channels_last.  Results must equal the
 NCHW path: the forward bitwise (same gather and epilogue arithmetic), and
 grad_weight bitwise (deterministic reduction over the same operands).  The
-atomically accumulated gradients match within 1e-3, and everything matches
-the float64 oracle within the dtype tolerance.  Problems outside the
+atomically accumulated gradients match within half the dtype tolerance, and
+everything matches the float64 oracle within the dtype tolerance.  Problems outside the
 tensor-core path run on NCHW copies and still return channels_last outputs.
 """
 import pytest
@@ -52,9 +52,11 @@ def test_channels_last_matches_nchw_and_oracle(name, dtype, cuda):
             assert g["input"].is_contiguous(memory_format=CL)
         assert torch.equal(out, out0), (in_cl, go_cl)
         assert torch.equal(g["weight"], g0["weight"]), (in_cl, go_cl)
+        # accumulated with fp32 atomics in run-dependent order: last-bit flips
+        # after rounding to 16 bits (a layout error would be of order 1)
         for k in ("input", "offset", "mask", "bias"):
             if k in g:
-                assert rel_err(to_np(g[k]), to_np(g0[k])) <= 1e-3, (k, in_cl, go_cl)
+                assert rel_err(to_np(g[k]), to_np(g0[k])) <= TOL[dtype] / 2, (k, in_cl, go_cl)
     st, pd, dl = T["stride"], T["padding"], T["dilation"]
     ref = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"], st, pd, dl,
