@@ -8,17 +8,20 @@
 // at::mm / at::bmm (mm:765-782) as the tcgen05 MMA, so the column buffer never
 // exists in memory.
 //
-// Warp roles (320 threads):
-//   warps 0-7  gather producers: each thread owns one pixel row of the A tile
-//              and half of its 64 channels; it reads the offset/mask of its
-//              (pixel, tap, offset group), loads the 4 bilinear corners as
-//              16-byte channel vectors from the channels-last copy of the
-//              input, blends them in fp32 and writes the 128-byte-swizzled A
-//              row to shared memory.  After the main loop the same warps are
-//              the epilogue: TMEM -> registers -> +bias -> NCHW store.
-//   warp 8     MMA issuer (one thread) and TMEM owner.
-//   warp 9     weight loader: one bulk copy (TMA engine) per K chunk of the
-//              pre-swizzled weight image; no multicast.
+// Warp roles (576 threads):
+//   warps 0-15  gather producers (gather_run, dcn_tc_common.cuh): 8 lanes per
+//               pixel row, one 16-byte channel vector each, two rows per lane;
+//               they read the offset/mask of the (pixel, tap, offset group),
+//               load the 4 bilinear corners from the channels-last input,
+//               blend them with packed 16-bit FMAs and write the
+//               128-byte-swizzled A rows to shared memory.  After the main
+//               loop the same warps are the epilogue: TMEM -> registers ->
+//               +bias -> NCHW (or channels-last) store.
+//   warp 16     MMA issuer (one thread) and TMEM owner.
+//   warp 17     lane 0: weight loader, one bulk copy (TMA engine) per K chunk
+//               of the pre-swizzled weight image; lane 1 (training): stores
+//               each full A stage to the saved column tiles with one bulk
+//               copy.  No multicast.
 // Every mbarrier wait is bounded (dcn_sm100.cuh): on expiry the kernel sets
 // the device status word and unwinds.
 #include <type_traits>
@@ -45,7 +48,7 @@ constexpr int LOAD_WARP = NPROD_WARPS + 1;
 constexpr int NTHREADS = (NPROD_WARPS + 2) * 32;
 
 // status codes recorded on a wait that expired
-constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16;
+constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16, ST_STORE = 17;
 
 struct FwdSmem {  // offsets within the 1024-aligned dynamic shared memory
   uint32_t a, b, bar, total;
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
     for (int s = 0; s < S; ++s) {
       mbar_init(a_full(s), NPROD);
       mbar_init(b_full(s), 1);
-      mbar_init(empty(s), 1);
+      mbar_init(empty(s), a.cols ? 2 : 1);  // MMA commit (+ column-tile store done reading)
     }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
@@ -131,15 +134,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
     // ------------------------------------------------ producers
     const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
     const PixelCtx pc[2] = {pixel_ctx(g, (long long)tile * BM + r0), pixel_ctx(g, (long long)tile * BM + r0 + 4)};
-    uint8_t* cols_tile = a.cols ? static_cast<uint8_t*>(a.cols) +
-                                      ((size_t)grp * gridDim.x + tile) * a.nkc * (size_t)A_STAGE_BYTES
-                                : nullptr;
     Ring ring{0, S, 0u};
     const bool ok = gather_run<T, LOGIT>(
         g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
-        [&](int i, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
+        [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
           t = smem + L.a + s * A_STAGE_BYTES;
-          gt = cols_tile ? cols_tile + (size_t)i * A_STAGE_BYTES : nullptr;
+          gt = nullptr;  // the saved column tile is stored from shared memory by the store lane
           eb = empty(s);
           fb = a_full(s);
         });
@@ -231,6 +231,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
       // copies still in flight must land before the CTA exits
       for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
         mbar_wait(b_full(i % S), (i / S) & 1, abort_flag, a.status, ST_LOAD);
+    } else if (lane == 1 && a.cols) {
+      // ---------------------------------------------- column-tile store (training)
+      // Each full A stage is already the saved tile's image: one bulk copy
+      // per chunk to `cols`, and the stage counts as empty once the copy has
+      // read it (second arrival on `empty`, next to the MMA's commit).
+      uint8_t* gbase = static_cast<uint8_t*>(a.cols) + ((size_t)grp * gridDim.x + tile) * a.nkc * (size_t)A_STAGE_BYTES;
+      for (int i = 0; i < a.nkc; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(a_full(s), (i / S) & 1, abort_flag, a.status, ST_STORE)) break;
+        bulk_s2g(gbase + (size_t)i * A_STAGE_BYTES, sbase + L.a + s * A_STAGE_BYTES, A_STAGE_BYTES);
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(empty(s));
+      }
+      bulk_wait_all();  // the tiles are in global memory before the CTA exits
     }
   }
 
