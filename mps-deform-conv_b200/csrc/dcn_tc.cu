@@ -137,9 +137,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
     Ring ring{0, S, 0u};
     const bool ok = gather_run<T, LOGIT>(
         g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
-        [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
-          t = smem + L.a + s * A_STAGE_BYTES;
-          gt = nullptr;  // the saved column tile is stored from shared memory by the store lane
+        [&](int s, uint8_t*& t, uint32_t& eb, uint32_t& fb) {
+          t = smem + L.a + s * A_STAGE_BYTES;  // saved as a column tile by the store lane (training)
           eb = empty(s);
           fb = a_full(s);
         });

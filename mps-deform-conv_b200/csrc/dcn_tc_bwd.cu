@@ -143,9 +143,8 @@ dcn_wgrad_tc_kernel(const WgradArgs a, const __grid_constant__ CUtensorMap tmap_
     for (int li = 0; li < nt && ok; ++li) {
       const PixelCtx pc[2] = {pixel_ctx(g, (long long)(t0 + li) * BM + r0),
                               pixel_ctx(g, (long long)(t0 + li) * BM + r0 + 4)};
-      auto stage_of = [&](int, int s, uint8_t*& t, uint8_t*& gt, uint32_t& eb, uint32_t& fb) {
+      auto stage_of = [&](int s, uint8_t*& t, uint32_t& eb, uint32_t& fb) {
         t = smem + L.b + s * A_STAGE_BYTES;
-        gt = nullptr;
         eb = b_empty(s);
         fb = b_full(s);
       };

@@ -216,9 +216,8 @@ __device__ __forceinline__ CornerSet32 corner_set32(const Geom& g, const PixelCt
 // tile.  The sampling points and the offset / mask loads are reused while
 // consecutive chunks share the tap and the offset group.  `ring` is the
 // stage ring position (advanced once per chunk);
-// `stage_of(i, s, tile, gtile, empty_bar, full_bar)` gives the shared-memory
-// tile of stage s, the global copy of the i-th tile of the run (or null) and
-// the barriers.  Returns false if a wait expired.  The input (B*H*W*C) and
+// `stage_of(s, tile, empty_bar, full_bar)` gives the shared-memory tile of
+// stage s and its barriers.  Returns false if a wait expired.  The input (B*H*W*C) and
 // offset / mask tensors (B * per-sample stride) hold fewer than 2^31 elements.
 template <typename T, bool LOGIT, class StageFn>
 __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ xh,
@@ -282,14 +281,9 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
       }
     }
     uint8_t* tile;
-    uint8_t* gtile;  // global copy of the tile image, or null
     uint32_t empty_bar, full_bar;
-    stage_of(i, ring.s, tile, gtile, empty_bar, full_bar);
+    stage_of(ring.s, tile, empty_bar, full_bar);
     const uint4 b0 = blend8<T>(v[0], cs[0].w), b1 = blend8<T>(v[1], cs[1].w);
-    if (gtile) {  // streaming stores: keep L2 for the gather
-      __stcs(reinterpret_cast<uint4*>(gtile + o0), b0);
-      __stcs(reinterpret_cast<uint4*>(gtile + o1), b1);
-    }
     if (!mbar_wait(empty_bar, ring.ph ^ 1u, abort_flag, status, code)) return false;
     *reinterpret_cast<uint4*>(tile + o0) = b0;
     *reinterpret_cast<uint4*>(tile + o1) = b1;

@@ -117,6 +117,40 @@ def test_head_layout_support_query_and_rejection_without_launching():
         assert "head layout" in lib.dcn_last_error().decode()
 
 
+def test_ex_layout_options_checked_without_launching():
+    """dcn_*_ex: channels-last layouts need the tensor-core path, channels-last
+    pointers must be 16-byte aligned, and plain options behave like the
+    training pair; every check here returns before anything is launched."""
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    nhwc = _abi.DcnExOptions(_abi.DCN_LAYOUT_NHWC, _abi.DCN_LAYOUT_NHWC, 0, 0)
+    plain = _abi.DcnExOptions(_abi.DCN_LAYOUT_NCHW, _abi.DCN_LAYOUT_NCHW, 0, 0)
+    bad_layout = _abi.DcnExOptions(7, _abi.DCN_LAYOUT_NCHW, 0, 0)
+    tc = _desc(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1),
+               use_mask=True)
+    f32 = _desc(input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1), use_mask=True)
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(nhwc), 0) == 1
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(nhwc), 1) == 1
+    assert lib.dcn_ex_supported(ctypes.byref(f32), ctypes.byref(nhwc), 0) == 0
+    assert lib.dcn_ex_supported(ctypes.byref(f32), ctypes.byref(plain), 1) == 1   # any problem, any path
+    assert lib.dcn_ex_supported(ctypes.byref(f32), None, 1) == 1
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(bad_layout), 0) == 0
+    p = ctypes.c_void_p(16)
+    rc = lib.dcn_deform_conv2d_forward_ex(ctypes.byref(f32), ctypes.byref(nhwc), p, p, p, p, None, p, None, 0,
+                                          None, 0, None)
+    assert rc == _abi.DCN_ERR_UNSUPPORTED
+    rc = lib.dcn_deform_conv2d_forward_ex(ctypes.byref(tc), ctypes.byref(nhwc), ctypes.c_void_p(18), p, p, p, None,
+                                          p, None, 0, None, 0, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT
+    assert "16-byte aligned" in lib.dcn_last_error().decode()
+    rc = lib.dcn_deform_conv2d_backward_ex(ctypes.byref(tc), ctypes.byref(nhwc), p, ctypes.c_void_p(34), p, p, p,
+                                           None, 0, p, p, p, p, None, None, 0, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT
+    rc = lib.dcn_deform_conv2d_forward_ex(ctypes.byref(tc), None, None, None, None, None, None, None, None, 0,
+                                          None, 0, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT and "NULL" in lib.dcn_last_error().decode()
+
+
 def test_torch_extension_imports():
     import mps_deform_conv
     lib = mps_deform_conv._get_lib()
