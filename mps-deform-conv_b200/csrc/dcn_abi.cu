@@ -263,7 +263,7 @@ int dcn_uses_tensor_cores(const dcn_conv_desc* d) {
 size_t dcn_forward_workspace_size(const dcn_conv_desc* d) {
   if (validate(d) != DCN_OK) return 0;
   const Geom g = make_geom(*d);
-  return tc_forward_supported(*d, g) ? tc_forward_workspace(*d, g) : 0;
+  return tc_forward_supported(*d, g) ? tc_forward_workspace(*d, g) : simt_forward_workspace(g);
 }
 
 static int forward_impl(const dcn_conv_desc* d, const void* input, const void* weight,
@@ -289,11 +289,15 @@ static int forward_impl(const dcn_conv_desc* d, const void* input, const void* w
     cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, saved, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward (tensor core)");
   }
+  const size_t need = simt_forward_workspace(g);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
   cudaError_t e = cudaSuccess;
   dispatch_dtype(d->dtype, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     e = simt_forward<T>(g, (const T*)input, (const T*)weight, (const T*)offset,
-                        (const T*)(d->use_mask ? mask : nullptr), (const T*)bias, (T*)output, st);
+                        (const T*)(d->use_mask ? mask : nullptr), (const T*)bias, (T*)output,
+                        need ? workspace : nullptr, st);
     return 0;
   });
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward");

@@ -13,9 +13,12 @@ struct SimtBackwardWs {
   void* goff_scratch;   // offset-grad sink when the caller wants only grad_mask
 };
 
+// Forward workspace: the K-split partial sums when the output tiles alone
+// would not fill one wave of the 148 SMs (0 otherwise).
+size_t simt_forward_workspace(const Geom& g);
 template <typename T>
 cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
-                         const T* bias, T* out, cudaStream_t st);
+                         const T* bias, T* out, void* workspace, cudaStream_t st);
 template <typename T>
 cudaError_t simt_im2col(const Geom& g, const T* x, const T* off, const T* msk, T* cols,
                         cudaStream_t st);

@@ -283,15 +283,65 @@ static inline int grid_for(long long n, int threads = 256) {
   return (int)(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
+// Forward K-split: split s of the reduction stores its partial output
+// part[s][g*Cog + m][n] (n = b*HWo + p); simt_fwd_reduce adds the splits in
+// order, plus bias, so the result does not depend on scheduling.
+struct SplitPartialEpilogue {
+  float* part; int splits, Co, Cog; long long P;
+  __device__ void operator()(int g, int m, int n, float acc) const {
+    const int s = blockIdx.z % splits;
+    part[((long long)s * Co + g * Cog + m) * P + n] = acc;
+  }
+};
+
+template <typename T>
+__global__ void simt_fwd_reduce_kernel(Geom g, const float* __restrict__ part, int splits,
+                                       const T* __restrict__ bias, T* __restrict__ out) {
+  const long long total = (long long)g.Co * g.P;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int oc = (int)(e / g.P);
+    const long long n = e - (long long)oc * g.P;
+    float acc = bias ? to_f(bias[oc]) : 0.f;
+    for (int s = 0; s < splits; ++s) acc += part[(long long)s * total + e];
+    const int b = (int)(n / g.HWo), p = (int)(n - (long long)b * g.HWo);
+    out[((long long)b * g.Co + oc) * g.HWo + p] = from_f<T>(acc);
+  }
+}
+
+static int simt_fwd_splits(const Geom& g) {
+  const long long tiles = ((g.P + SG_BN - 1) / SG_BN) * ((g.Cog + SG_BM - 1) / SG_BM) * g.G;
+  if (tiles == 0 || tiles >= 148) return 1;  // empty batch, or at least one wave
+  const int ksteps = (g.Cig * g.T + SG_BK - 1) / SG_BK;
+  int splits = (int)((148 + tiles - 1) / tiles);
+  if (splits > ksteps / 4) splits = ksteps / 4;  // at least 4 K steps per split
+  return splits < 2 ? 1 : splits;
+}
+
+size_t simt_forward_workspace(const Geom& g) {
+  const int splits = simt_fwd_splits(g);
+  return splits > 1 ? sizeof(float) * (size_t)splits * g.Co * g.P : 0;
+}
+
 // ---------------------------------------------------------------- host side
 template <typename T>
 cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
-                         const T* bias, T* out, cudaStream_t st) {
+                         const T* bias, T* out, void* workspace, cudaStream_t st) {
   const int Kg = g.Cig * g.T;
   WeightRowLoader<T> la{w, g.Cog, Kg};
   ColumnLoader<T> lb{g, x, off, msk};
-  ForwardEpilogue<T> ep{g, bias, out};
-  return launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, 1, st);
+  const int splits = simt_fwd_splits(g);
+  if (splits == 1 || !workspace) {
+    ForwardEpilogue<T> ep{g, bias, out};
+    return launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, 1, st);
+  }
+  float* part = static_cast<float*>(workspace);
+  SplitPartialEpilogue ep{part, splits, g.Co, g.Cog, g.P};
+  cudaError_t e = launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, splits, st);
+  if (e != cudaSuccess) return e;
+  KernelScope ks("simt_fwd_reduce", st);
+  simt_fwd_reduce_kernel<T><<<grid_for((long long)g.Co * g.P), 256, 0, st>>>(g, part, splits, bias, out);
+  return cudaGetLastError();
 }
 
 template <typename T>
@@ -388,7 +438,7 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
 // ---------------------------------------------------------------- instances
 #define DCN_SIMT_INSTANCES(T)                                                                    \
   template cudaError_t simt_forward<T>(const Geom&, const T*, const T*, const T*, const T*,      \
-                                       const T*, T*, cudaStream_t);                              \
+                                       const T*, T*, void*, cudaStream_t);                       \
   template cudaError_t simt_im2col<T>(const Geom&, const T*, const T*, const T*, T*,            \
                                       cudaStream_t);                                             \
   template cudaError_t simt_col2im<T, T>(const Geom&, const T*, const T*, const T*, float*,     \

@@ -77,6 +77,18 @@ def test_workspace_sizes_are_host_queries():
     assert lib.dcn_backward_input_workspace_size(ctypes.byref(d)) == 2 * 64 * 16 * 16 * 4
     bad = _desc(stride=(0, 0))
     assert lib.dcn_backward_workspace_size(ctypes.byref(bad)) == 0
+    # every query of every path, on every dtype, including an empty batch
+    for dt in (_abi.DCN_FLOAT32, _abi.DCN_FLOAT16, _abi.DCN_BFLOAT16):
+        for shape in ((0, 64, 16, 16), (1, 64, 16, 16), (2, 4, 5, 6)):
+            q = _desc(dtype=dt, input_shape=shape, weight_shape=(64 if shape[1] == 64 else 4, shape[1], 3, 3),
+                      padding=(1, 1), use_mask=True)
+            for fn in ("dcn_forward_workspace_size", "dcn_backward_workspace_size",
+                       "dcn_backward_input_workspace_size", "dcn_saved_state_bytes"):
+                assert getattr(lib, fn)(ctypes.byref(q)) >= 0
+            assert lib.dcn_head_supported(ctypes.byref(q)) in (0, 1)
+    # an fp32 problem whose output tiles fill less than a wave splits K in the forward
+    small = _desc(input_shape=(1, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1))
+    assert lib.dcn_forward_workspace_size(ctypes.byref(small)) == 9 * 64 * 256 * 4
 
 
 def test_forward_rejects_null_and_small_workspace_without_launching():

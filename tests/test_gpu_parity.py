@@ -6,6 +6,8 @@ Tolerance: normwise relative error (tests/_util.rel_err) <= 1e-4 for fp32 and
 <= 1e-2 for fp16/bf16, per output and per gradient.  For fp16/bf16 the oracle
 runs on the same rounded inputs the GPU sees.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -127,6 +129,31 @@ def test_empty_batch(cuda):
     assert tuple(out.shape) == d["output"].shape
     out.sum().backward()
     assert torch.count_nonzero(w.grad) == 0 and torch.count_nonzero(b.grad) == 0
+
+
+@pytest.mark.parametrize("shape", [(1, 64, 16, 16, 64, 1), (2, 32, 12, 10, 48, 2)])
+def test_simt_forward_k_split_vs_oracle(shape, cuda):
+    """fp32 problems whose output tiles fill less than one wave split the
+    reduction over K; the splits are added in a fixed order, so the forward
+    stays deterministic and matches the oracle."""
+    from mps_deform_conv import _abi
+    B, C, H, W, Co, G = shape
+    g = torch.Generator().manual_seed(53)
+    x = torch.randn(B, C, H, W, generator=g)
+    w = torch.randn(Co, C // G, 3, 3, generator=g) / np.sqrt(C // G * 9)
+    off = torch.randn(B, 18, H, W, generator=g) * 1.5
+    m = torch.sigmoid(torch.randn(B, 9, H, W, generator=g))
+    b = torch.randn(Co, generator=g) * 0.1
+    d = _abi.desc_for(x, w, off, (1, 1), (1, 1), (1, 1), m)
+    lib = _abi.load()
+    assert lib.dcn_forward_workspace_size(ctypes.byref(d)) > 0  # the split partial sums
+    dev = [t.to(cuda) for t in (x, off, w, b, m)]
+    a = _abi.call_forward(dev[0], dev[1], dev[2], dev[3], (1, 1), (1, 1), (1, 1), dev[4])
+    a2 = _abi.call_forward(dev[0], dev[1], dev[2], dev[3], (1, 1), (1, 1), (1, 1), dev[4])
+    torch.cuda.synchronize()
+    assert torch.equal(a, a2)
+    ref = oracle.forward(x, off, w, b, (1, 1), (1, 1), (1, 1), m)
+    assert rel_err(to_np(a), ref) <= TOL["float32"]
 
 
 def test_device_status_clean_after_runs(cuda):
