@@ -129,15 +129,6 @@ struct ColumnLoader {  // B(k, n) = col[(g*Cig + k/T)*T + k%T][n]   (forward)
   }
 };
 template <typename T>
-struct ColumnLoaderPK {  // B(px, n=k) = col[(g*Cig + k/T)*T + k%T][px]   (wgrad)
-  Geom geo; const T* x; const T* off; const T* msk;
-  __device__ float operator()(int g, int px, int k) const {
-    const int b = px / geo.HWo, p = px - b * geo.HWo;
-    const int cl = k / geo.T, t = k - cl * geo.T;
-    return column_value(geo, x, off, msk, b, g * geo.Cig + cl, t, p);
-  }
-};
-template <typename T>
 struct GradOutLoaderCN {  // B(co, n=px) = gO[b][g*Cog + co][p]   (dgrad)
   Geom geo; const T* go;
   __device__ float operator()(int g, int co, int n) const {
@@ -152,6 +143,14 @@ struct GradOutLoaderPM {  // A(px, m=co) = gO[b][g*Cog + co][p]   (wgrad)
     const int b = px / geo.HWo, p = px - b * geo.HWo;
     return to_f(go[((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p]);
   }
+};
+struct ColumnBufferLoader {  // B(k, n) = cols[(g*Kg + k)][n]   (forward, materialized columns)
+  const float* cols; int Kg; long long P;
+  __device__ float operator()(int g, int k, int n) const { return cols[((long long)g * Kg + k) * P + n]; }
+};
+struct ColumnBufferLoaderPK {  // B(px, n=k) = cols[(g*Kg + k)][px]   (wgrad, materialized columns)
+  const float* cols; int Kg; long long P;
+  __device__ float operator()(int g, int px, int k) const { return cols[((long long)g * Kg + k) * P + px]; }
 };
 template <typename T>
 struct ForwardEpilogue {  // out[b][g*Cog + m][p] = acc + bias
@@ -177,16 +176,26 @@ struct AtomicWeightEpilogue {  // gW32[(g*Cog + m)*Kg + n] += acc
 };
 
 // ---------------------------------------------------------------- kernels
-template <typename T>
-__global__ void im2col_kernel(Geom g, const T* __restrict__ x, const T* __restrict__ off,
-                              const T* __restrict__ msk, T* __restrict__ cols) {
-  const long long total = (long long)g.C * g.T * g.P;
+// Column buffer with one sample per (pixel, tap, offset group): thread e
+// = (o, t, n) computes the sampling point once and writes the rows
+// (o*cpo + c)*T + t of all the group's channels (coalesced over pixels n).
+template <typename T, typename TC>
+__global__ void im2col_og_kernel(Geom g, const T* __restrict__ x, const T* __restrict__ off,
+                                 const T* __restrict__ msk, TC* __restrict__ cols) {
+  const long long total = (long long)g.OG * g.T * g.P;
+  const long long row_stride = (long long)g.T * g.P;  // channel c -> c + 1
+  const long long plane = (long long)g.H * g.W;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
        e += (long long)gridDim.x * blockDim.x) {
-    const long long row = e / g.P, n = e - row * g.P;
-    const int c = (int)(row / g.T), t = (int)(row - (long long)c * g.T);
+    const long long r = e / g.P, n = e - r * g.P;
+    const int o = (int)(r / g.T), t = (int)(r - (long long)o * g.T);
     const int b = (int)(n / g.HWo), p = (int)(n - (long long)b * g.HWo);
-    cols[e] = from_f<T>(column_value(g, x, off, msk, b, c, t, p));
+    float m;
+    const SamplePos sp = sample_point(g, off, msk, b, o, t, p, &m);
+    const Corners cs = corners_of(sp, g.H, g.W);
+    const T* src = x + ((long long)b * g.C + (long long)o * g.cpo) * plane;
+    TC* dst = cols + ((long long)o * g.cpo * g.T + t) * g.P + n;
+    for (int c = 0; c < g.cpo; ++c) dst[(long long)c * row_stride] = from_f<TC>(m * bilinear(src + (long long)c * plane, cs));
   }
 }
 
@@ -318,9 +327,19 @@ static int simt_fwd_splits(const Geom& g) {
   return splits < 2 ? 1 : splits;
 }
 
+// The forward materializes fp32 columns (one sample per pixel, tap and offset
+// group, im2col_og_kernel) when that kernel has at least a wave of threads
+// (148 x 256) and the columns take at most 1 GiB; other problems gather inside
+// the GEMM's operand loader.
+static size_t simt_fwd_cols_bytes(const Geom& g) {
+  const size_t b = sizeof(float) * (size_t)g.C * g.T * (size_t)g.P;
+  const long long threads = (long long)g.OG * g.T * g.P;
+  return (threads >= 148 * 256 && b <= (size_t(1) << 30)) ? b : 0;
+}
+
 size_t simt_forward_workspace(const Geom& g) {
   const int splits = simt_fwd_splits(g);
-  return splits > 1 ? sizeof(float) * (size_t)splits * g.Co * g.P : 0;
+  return ws_align(simt_fwd_cols_bytes(g)) + (splits > 1 ? sizeof(float) * (size_t)splits * g.Co * g.P : 0);
 }
 
 // ---------------------------------------------------------------- host side
@@ -329,16 +348,26 @@ cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, co
                          const T* bias, T* out, void* workspace, cudaStream_t st) {
   const int Kg = g.Cig * g.T;
   WeightRowLoader<T> la{w, g.Cog, Kg};
-  ColumnLoader<T> lb{g, x, off, msk};
-  const int splits = simt_fwd_splits(g);
-  if (splits == 1 || !workspace) {
-    ForwardEpilogue<T> ep{g, bias, out};
-    return launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, 1, st);
+  const size_t cols_bytes = workspace ? simt_fwd_cols_bytes(g) : 0;
+  float* cols = cols_bytes ? static_cast<float*>(workspace) : nullptr;
+  const int splits = workspace ? simt_fwd_splits(g) : 1;
+  float* part = splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + ws_align(cols_bytes)) : nullptr;
+  cudaError_t e;
+  if (cols) {
+    KernelScope ks("im2col_og", st);
+    im2col_og_kernel<T, float><<<grid_for((long long)g.OG * g.T * g.P), 256, 0, st>>>(g, x, off, msk, cols);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  float* part = static_cast<float*>(workspace);
-  SplitPartialEpilogue ep{part, splits, g.Co, g.Cog, g.P};
-  cudaError_t e = launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, splits, st);
-  if (e != cudaSuccess) return e;
+  auto gemm = [&](const auto& ep, int nsplit) {
+    if (cols) {
+      ColumnBufferLoader lb{cols, Kg, g.P};
+      return launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, nsplit, st);
+    }
+    ColumnLoader<T> lb{g, x, off, msk};
+    return launch_simt_gemm<false, false>("simt_fwd_gemm", la, lb, ep, g.Cog, (int)g.P, Kg, g.G, nsplit, st);
+  };
+  if (!part) return gemm(ForwardEpilogue<T>{g, bias, out}, 1);
+  if ((e = gemm(SplitPartialEpilogue{part, splits, g.Co, g.Cog, g.P}, splits)) != cudaSuccess) return e;
   KernelScope ks("simt_fwd_reduce", st);
   simt_fwd_reduce_kernel<T><<<grid_for((long long)g.Co * g.P), 256, 0, st>>>(g, part, splits, bias, out);
   return cudaGetLastError();
@@ -350,7 +379,7 @@ cudaError_t simt_im2col(const Geom& g, const T* x, const T* off, const T* msk, T
   const long long total = (long long)g.C * g.T * g.P;
   if (total == 0) return cudaSuccess;
   KernelScope ks("im2col", st);
-  im2col_kernel<T><<<grid_for(total), 256, 0, st>>>(g, x, off, msk, cols);
+  im2col_og_kernel<T, T><<<grid_for((long long)g.OG * g.T * g.P), 256, 0, st>>>(g, x, off, msk, cols);
   return cudaGetLastError();
 }
 
@@ -407,8 +436,15 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
     GradOutLoaderPM<T> la{g, go};
-    ColumnLoaderPK<T> lb{g, x, off, msk};
     AtomicWeightEpilogue ep{gw32, g.Cog, Kg};
+    // the columns, one sample per (pixel, tap, offset group), in the column
+    // gradient's buffer (free until the dgrad GEMM below writes it)
+    {
+      KernelScope ks("im2col_og", st);
+      im2col_og_kernel<T, float><<<grid_for((long long)g.OG * g.T * g.P), 256, 0, st>>>(g, x, off, msk, ws.gcol);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    ColumnBufferLoaderPK lb{ws.gcol, Kg, g.P};
     if ((e = launch_simt_gemm<true, true>("simt_wgrad_gemm", la, lb, ep, g.Cog, Kg, (int)g.P, g.G, (int)splits, st)) != cudaSuccess)
       return e;
     if (ws.gw32 && (e = convert_f32<T>(ws.gw32, gw, (long long)g.Co * Kg, st)) != cudaSuccess) return e;

@@ -86,9 +86,13 @@ def test_workspace_sizes_are_host_queries():
                        "dcn_backward_input_workspace_size", "dcn_saved_state_bytes"):
                 assert getattr(lib, fn)(ctypes.byref(q)) >= 0
             assert lib.dcn_head_supported(ctypes.byref(q)) in (0, 1)
-    # an fp32 problem whose output tiles fill less than a wave splits K in the forward
+    # an fp32 problem whose output tiles fill less than a wave splits K in the
+    # forward (9 partials here); with at least a wave of (pixel, tap, offset
+    # group) threads the forward also materializes fp32 columns [C*T][P]
     small = _desc(input_shape=(1, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1))
     assert lib.dcn_forward_workspace_size(ctypes.byref(small)) == 9 * 64 * 256 * 4
+    c2 = _desc(input_shape=(2, 128, 64, 64), weight_shape=(128, 128, 3, 3), padding=(1, 1), use_mask=True)
+    assert lib.dcn_forward_workspace_size(ctypes.byref(c2)) == 128 * 9 * 8192 * 4
 
 
 def test_forward_rejects_null_and_small_workspace_without_launching():
