@@ -167,6 +167,28 @@ def test_ex_layout_options_checked_without_launching():
     assert rc == _abi.DCN_ERR_INVALID_ARGUMENT and "NULL" in lib.dcn_last_error().decode()
 
 
+@pytest.mark.parametrize("kw,expect", [
+    (dict(), 1),                                                   # bf16, 64 -> 64, og 1
+    (dict(dtype=0), 0),                                            # fp32: SIMT
+    (dict(dtype=1), 1),                                            # fp16
+    (dict(input_shape=(2, 96, 16, 16), weight_shape=(64, 96, 3, 3)), 0),   # C/G not a multiple of 64
+    (dict(weight_shape=(48, 64, 3, 3)), 0),                        # C_out/G not a multiple of 32
+    (dict(weight_shape=(512, 64, 3, 3)), 1),                       # C_out/G = 512: forward
+    (dict(n_offset_grps=16), 0),                                   # 4 channels per offset group
+    (dict(n_offset_grps=8), 1),                                    # 8 channels per offset group
+    (dict(input_shape=(2, 128, 16, 16), weight_shape=(128, 64, 3, 3), n_weight_grps=2), 1),
+])
+def test_tensor_core_dispatch_rules(kw, expect):
+    """The dispatch conditions of the tensor-core path (a host query)."""
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    base = dict(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1),
+                use_mask=True)
+    base.update(kw)
+    d = _desc(**base)
+    assert lib.dcn_uses_tensor_cores(ctypes.byref(d)) == expect
+
+
 def test_torch_extension_imports():
     import mps_deform_conv
     lib = mps_deform_conv._get_lib()
