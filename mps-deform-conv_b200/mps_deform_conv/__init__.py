@@ -17,6 +17,8 @@ from typing import Optional, Tuple
 import torch
 from torch import Tensor, nn
 
+from . import ops as _ops
+
 __version__ = "0.2.2"
 
 # Thread-safe library loading (reference __init__.py:17-55)
@@ -342,8 +344,13 @@ def deform_conv2d(
 
     Raises:
         ValueError: If input is not on a CUDA device or parameters are invalid.
+
+    While a compiler traces it, or on meta tensors, the call goes through the
+    registered operators of ``mps_deform_conv.ops`` (fake implementations for
+    shapes, autograd wired to the fused backward).
     """
-    if not input.device.type == "cuda":
+    traced = input.device.type == "meta" or torch.compiler.is_compiling()
+    if not (input.device.type == "cuda" or traced):
         raise ValueError(f"Input must be on CUDA device, got {input.device}")
     stride, padding, dilation = _pair(stride), _pair(padding), _pair(dilation)
     kernel_h, kernel_w = weight.size(2), weight.size(3)
@@ -356,6 +363,9 @@ def deform_conv2d(
         in_channels, out_channels, offset_channels, kernel_h, kernel_w, weight_in_channels
     )
     use_mask = mask is not None
+    if traced:
+        return _ops.traced_deform_conv2d(input, offset, weight, bias, stride, padding, dilation, mask,
+                                         n_weight_grps, n_offset_grps)
     return _DeformConv2dFunction.apply(
         input, offset, weight, bias,
         stride, padding, dilation, mask,
@@ -462,6 +472,8 @@ class ModulatedDeformConv2d(nn.Module):
         nn.init.zeros_(self.offset_conv.bias)
 
     def _fused_head(self, input: Tensor, offset_mask: Tensor) -> bool:
+        if torch.compiler.is_compiling():  # traced: the composition below, through the registered operators
+            return False
         if not (_head_fusion and input.is_cuda and input.dim() == 4 and
                 input.dtype == offset_mask.dtype == self.weight.dtype and
                 (self.bias is None or self.bias.dtype == input.dtype)):
