@@ -45,7 +45,7 @@ constexpr int NPROD_WARPS = GATHER_WARPS;
 constexpr int NPROD = GATHER_THREADS;
 constexpr int MMA_WARP = NPROD_WARPS;
 constexpr int LOAD_WARP = NPROD_WARPS + 1;
-constexpr int NTHREADS = (NPROD_WARPS + 2) * 32;
+constexpr int NTHREADS = (LOAD_WARP + 1) * 32;  // producers, MMA warp, loader warp
 
 // status codes recorded on a wait that expired
 constexpr int ST_PROD = 11, ST_MMA_A = 12, ST_MMA_B = 13, ST_LOAD = 14, ST_EPI = 15, ST_DRAIN = 16, ST_STORE = 17;

@@ -400,7 +400,7 @@ dcn_wgrad_cols_tc_kernel(const WgradArgs a, const void* __restrict__ cols,
 constexpr int D_EPI_WARPS = 16;      // 4 groups of 4 warps, one group per TMEM buffer
 constexpr int D_MMA_WARP = 16;
 constexpr int D_LOAD_WARP = 17;
-constexpr int D_NTHREADS = 576;
+constexpr int D_NTHREADS = (D_LOAD_WARP + 1) * 32;  // 576: epilogue warps, MMA warp, loader warp
 constexpr int D_NBUF = 4;            // TMEM gcol buffers of 64 columns
 
 struct DgradArgs {
