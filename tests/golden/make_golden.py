@@ -37,7 +37,8 @@ CASES = {
 }
 
 
-def make_case(name, spec, seed):
+def case_arrays(spec, seed):
+    """The fixture arrays of one case (inputs, output, gradients, geometry)."""
     (B, C, H, W, Co, groups, og, (kh, kw), stride, pad, dil, use_mask, use_bias, okind) = spec
     g = torch.Generator().manual_seed(seed)
     Ho = (H + 2 * pad[0] - (dil[0] * (kh - 1) + 1)) // stride[0] + 1
@@ -97,12 +98,17 @@ def make_case(name, spec, seed):
         arrays["bias"] = bias.numpy()
         if B > 0:
             arrays["grad_bias"] = bs.grad.numpy()
-    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)
+    return arrays
+
+
+def seeds():
+    """name -> seed: cases in sorted order from 1000."""
+    return {name: 1000 + i for i, name in enumerate(sorted(CASES))}
 
 
 def main():
-    for i, (name, spec) in enumerate(sorted(CASES.items())):
-        make_case(name, spec, seed=1000 + i)
+    for name, seed in seeds().items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **case_arrays(CASES[name], seed))
         print("wrote", name)
 
 
