@@ -141,11 +141,14 @@ DCN_API int dcn_deform_conv2d_backward_input(const dcn_conv_desc *desc, const vo
  * dcn_deform_conv2d_backward_input, without the workspace: the fp32
  * accumulator for fp16/bf16 data is a fixed 8 MiB array in device memory
  * that every GPU which loads the library holds until the process exits.
- *   - Limit: grad_input (B*C*H*W) may have at most 2,097,152 elements;
- *     larger problems return DCN_ERR_UNSUPPORTED.
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *   - Limit: for fp16/bf16, grad_input (B*C*H*W) may have at most 2,097,152
+ *     elements; larger problems return DCN_ERR_UNSUPPORTED.  fp32 data
+ *     accumulates in grad_input itself, never uses the array and has no
+ *     such limit.
+ *   - The first fp16/bf16 call on a device looks up the array's device
+ *     address (cudaGetSymbolAddress) with that device current, and looks it
+ *     up again after the device's context was reset (cudaDeviceReset); make
+ *     that first call before any stream capture.
  *   - All calls share the one array and each call clears the part it uses.
  *     Calls that overlap on the GPU (other streams, other host threads, same
  *     device) race on it: issue them on one stream.

@@ -669,11 +669,12 @@ int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void
   if (r != DCN_OK) return r;
   const Geom g = make_geom(dd);
   const long long n = (long long)g.B * g.C * g.H * g.W;
-  if (n > noalloc_max_elems())
+  // fp32 accumulates in grad_input itself; only fp16/bf16 use the fixed array
+  if (dd.dtype != DCN_FLOAT32 && n > noalloc_max_elems())
     return fail(DCN_ERR_UNSUPPORTED,
                 "backward_input_noalloc: grad_input has %lld elements, more than the %lld this "
-                "allocation-free entry point supports; use dcn_deform_conv2d_backward_input with a "
-                "workspace",
+                "allocation-free entry point supports for fp16/bf16; use "
+                "dcn_deform_conv2d_backward_input with a workspace",
                 n, noalloc_max_elems());
   if (n == 0) return ok();
   if (!grad_col || !offset || !grad_input || (dd.use_mask && !mask))

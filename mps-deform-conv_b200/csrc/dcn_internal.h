@@ -42,6 +42,19 @@ cudaError_t noalloc_backward_input_dispatch(int dtype, const Geom& g, const void
                                             const void* off, const void* msk, void* gin,
                                             cudaStream_t st);
 
+// Device address of a __device__ variable on the current device.  `symbol` is
+// the variable's host-side stand-in (its name in host code), which is not a
+// device address.  The address is looked up with cudaGetSymbolAddress, with
+// the device current, the first time a (device, CUDA context) pair asks, and
+// cached per device; a different current context on that device (a new
+// primary context after cudaDeviceReset) gets a fresh lookup.  Thread-safe.
+struct DeviceSymbolCache {
+  static constexpr int kMaxDevices = 64;
+  void* ctx[kMaxDevices] = {};
+  void* ptr[kMaxDevices] = {};
+};
+cudaError_t device_symbol_address(DeviceSymbolCache& cache, const void* symbol, void** out);
+
 // Counts kernel launches made by this library (dcn_launch_count()).
 void note_launch(int n = 1);
 

@@ -14,8 +14,9 @@
 // exits.  Host code cannot use the array's name as a device address (in host
 // code it names a host-side stand-in), so the device address is looked up
 // with cudaGetSymbolAddress, once per device, with that device current, on
-// the first call made on that device.
-#include <mutex>
+// the first fp16/bf16 call made on that device (and again after the device's
+// context was reset).  fp32 data accumulates straight into grad_input and
+// never uses the array, so fp32 problems have no size limit here.
 #include <type_traits>
 
 #include "dcn_internal.h"
@@ -23,28 +24,18 @@
 namespace dcn {
 
 constexpr long long NOALLOC_MAX_ELEMS = 2LL * 1024 * 1024;  // grad_input elements (8 MiB of fp32)
-constexpr int NOALLOC_MAX_DEVICES = 64;
 
 static __device__ __align__(256) float g_noalloc_accum[NOALLOC_MAX_ELEMS];
 
-static std::mutex g_noalloc_mu;
-static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES];
-
-// Device address of the accumulator on the current device (set up on first use).
+// Device address of the accumulator on the current device: looked up on the
+// first call made on a device (with that device current) and again whenever
+// the device's CUDA context has changed since (cudaDeviceReset).
 static cudaError_t noalloc_accum_ptr(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_accum);
-    if (e != cudaSuccess) return e;
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
-  return cudaSuccess;
+  static DeviceSymbolCache cache;
+  void* p = nullptr;
+  const cudaError_t e = device_symbol_address(cache, &g_noalloc_accum, &p);
+  *out = static_cast<float*>(p);
+  return e;
 }
 
 long long noalloc_max_elems() { return NOALLOC_MAX_ELEMS; }
@@ -67,8 +58,10 @@ cudaError_t noalloc_backward_input_dispatch(int dtype, const Geom& g, const void
                                             const void* off, const void* msk, void* gin,
                                             cudaStream_t st) {
   float* accum = nullptr;
-  cudaError_t e = noalloc_accum_ptr(&accum);
-  if (e != cudaSuccess) return e;
+  if (dtype != DCN_FLOAT32) {
+    const cudaError_t e = noalloc_accum_ptr(&accum);
+    if (e != cudaSuccess) return e;
+  }
   switch (dtype) {
     case DCN_FLOAT32:
       return noalloc_backward_input<float>(g, (const float*)gcol, (const float*)off,

@@ -24,6 +24,7 @@
 //               copy.  No multicast.
 // Every mbarrier wait is bounded (dcn_sm100.cuh): on expiry the kernel sets
 // the device status word and unwinds.
+#include <mutex>
 #include <type_traits>
 
 #include "dcn_layout.cuh"
@@ -355,13 +356,50 @@ SavedLayout saved_layout(const Geom& g) {
   return L;
 }
 
-int* tc_status_ptr() {
-  static int* p = nullptr;  // one device address per process (first device that asks)
-  if (!p) {
-    void* q = nullptr;
-    if (cudaGetSymbolAddress(&q, sm100::g_dcn_status) == cudaSuccess) p = static_cast<int*>(q);
+// Current CUDA context of the calling thread (null when none is current or
+// the driver entry point is missing).
+static void* current_context() {
+  typedef int (*CtxGetCurrentFn)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(f);
+  });
+  void* c = nullptr;
+  if (fn && fn(&c) != 0) c = nullptr;
+  return c;
+}
+
+cudaError_t device_symbol_address(DeviceSymbolCache& cache, const void* symbol, void** out) {
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= DeviceSymbolCache::kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  void* ctx = current_context();
+  if (cache.ptr[dev] && ctx && ctx == cache.ctx[dev]) {
+    *out = cache.ptr[dev];
+    return cudaSuccess;
   }
-  return p;
+  void* p = nullptr;
+  if ((e = cudaGetSymbolAddress(&p, symbol)) != cudaSuccess) return e;
+  cache.ptr[dev] = p;
+  cache.ctx[dev] = current_context();  // the lookup made the device's context current
+  *out = p;
+  return cudaSuccess;
+}
+
+cudaError_t tc_status_ptr(int** out) {
+  static DeviceSymbolCache cache;  // one address per device
+  void* p = nullptr;
+  cudaError_t e = device_symbol_address(cache, &sm100::g_dcn_status, &p);
+  *out = static_cast<int*>(p);
+  return e;
 }
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
@@ -421,8 +459,7 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   FwdArgs a;
   a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.bias = bias; a.out = out; a.wsw = wsw;
   a.cols = saved ? static_cast<char*>(saved) + SV.cols : nullptr;
-  a.status = tc_status_ptr();
-  if (!a.status) return cudaErrorSymbolNotFound;
+  if ((e = tc_status_ptr(&a.status)) != cudaSuccess) return e;
   a.g = g;
   a.nkc = (g.Cig / BK) * g.T;
   a.stages = pick_stages(g.Cog);

@@ -1330,8 +1330,11 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   float* gmsk32 = g.msk_logit ? goff32 + (size_t)2 * g.OG * g.T * g.HWo : reinterpret_cast<float*>(ws + L.gmsk32);
   float* gwp = reinterpret_cast<float*>(ws + L.gwp);
   float* gb32 = reinterpret_cast<float*>(ws + L.gb32);
-  int* status = tc_status_ptr();
-  if (!status) return cudaErrorSymbolNotFound;
+  int* status = nullptr;
+  {
+    const cudaError_t se = tc_status_ptr(&status);
+    if (se != cudaSuccess) return se;
+  }
   const bool need_d = gin || goff || gmsk;
   const int KB = (g.Cog + 63) / 64;
   const int nkc = (g.Cig / BK) * g.T;

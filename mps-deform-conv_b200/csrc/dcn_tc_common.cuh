@@ -335,7 +335,7 @@ __host__ __device__ constexpr uint32_t idesc_f16_major(int M, int N, bool ab_bf1
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
                   uint32_t box_rows, uint32_t box_cols);
 
-// Host: device address of the status word (null on failure).
-int* tc_status_ptr();
+// Host: device address of the status word on the current device.
+cudaError_t tc_status_ptr(int** out);
 
 }  // namespace dcn
