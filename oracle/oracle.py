@@ -157,3 +157,28 @@ def col2im_coord(grad_columns, input, offset, mask, kernel_h, kernel_w, stride=(
     _load().dcn_oracle_col2im_coord(ctypes.byref(s), _ptr(gc), _ptr(x), _ptr(off), _ptr(m),
                                     _ptr(goff), _ptr(gm))
     return goff, gm
+
+
+def param_grads(grad_out, input, offset, weight, stride=(1, 1), padding=(0, 0), dilation=(1, 1),
+                mask=None):
+    """float64 (grad_weight, grad_bias) for problems too large for the scalar
+    loops of dcn_oracle_backward.  Same arithmetic, per weight group
+    (mps_deform_conv/__init__.py:266-286, with the per-group products the
+    forward's grouped bmm implies): the columns come from the C restatement of
+    deformable_im2col, grad_weight_g = grad_out_g . columns_g^T is a float64
+    numpy (BLAS) product and grad_bias is the sum of grad_out over batch and
+    pixels."""
+    x, off, w, m = _arr(input), _arr(offset), _arr(weight), _arr(mask)
+    go = _arr(grad_out)
+    Co, cig, kh, kw = w.shape
+    G = x.shape[1] // cig
+    og = _og_of(off, w)
+    cols = im2col(x, off, m, kh, kw, _pair(stride), _pair(padding), _pair(dilation), og)
+    P = cols.shape[1]
+    go2 = np.ascontiguousarray(go.transpose(1, 0, 2, 3).reshape(Co, P))
+    K = cig * kh * kw
+    cog = Co // G
+    gw = np.empty((Co, K), dtype=np.float64)
+    for g in range(G):
+        gw[g * cog:(g + 1) * cog] = go2[g * cog:(g + 1) * cog] @ cols[g * K:(g + 1) * K].T
+    return gw.reshape(w.shape), go2.sum(axis=1)

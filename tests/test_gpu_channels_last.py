@@ -12,7 +12,7 @@ tensor-core path run on NCHW copies and still return channels_last outputs.
 import pytest
 import torch
 
-from _util import TOL, rel_err, to_np
+from _util import TOL, assert_close, rel_err, to_np
 from oracle import oracle
 from test_gpu_tc import SHAPES, _make
 
@@ -62,10 +62,10 @@ def test_channels_last_matches_nchw_and_oracle(name, dtype, cuda):
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"], st, pd, dl,
                                                 T["mask"], T["bias"] is not None)
     tol = TOL[dtype]
-    assert rel_err(to_np(out), ref) <= tol
-    assert rel_err(to_np(g["input"]), rgi) <= tol
-    assert rel_err(to_np(g["offset"]), rgoff) <= tol
-    assert rel_err(to_np(g["weight"]), rgw) <= tol
+    assert_close(out, ref, dtype, 'out')
+    assert_close(g["input"], rgi, dtype, 'g["input"]')
+    assert_close(g["offset"], rgoff, dtype, 'g["offset"]')
+    assert_close(g["weight"], rgw, dtype, 'g["weight"]')
 
 
 def test_channels_last_fp32_falls_back_and_keeps_format(cuda):

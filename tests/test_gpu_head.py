@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import TOL, rel_err, to_np
+from _util import TOL, assert_close, rel_err, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -67,12 +67,12 @@ def test_head_forward_backward_vs_oracle(name, dtype, keep_saved, cuda):
     m_np = to_np(m)
     rgom = np.concatenate([rgoff, rgm * m_np * (1.0 - m_np)], axis=1)
     tol = TOL[dtype]
-    assert rel_err(to_np(out), ref) <= tol
-    assert rel_err(to_np(gi), rgi) <= tol
-    assert rel_err(to_np(gw), rgw) <= tol
-    assert rel_err(to_np(gb), rgb) <= tol
-    assert rel_err(to_np(gom[:, :n_off]), rgoff) <= tol
-    assert rel_err(to_np(gom[:, n_off:]), rgom[:, n_off:]) <= tol
+    assert_close(out, ref, dtype, 'out')
+    assert_close(gi, rgi, dtype, 'gi')
+    assert_close(gw, rgw, dtype, 'gw')
+    assert_close(gb, rgb, dtype, 'gb')
+    assert_close(gom[:, :n_off], rgoff, dtype, 'gom[:, :n_off]')
+    assert_close(gom[:, n_off:], rgom[:, n_off:], dtype, 'gom[:, n_off:]')
 
 
 @pytest.mark.parametrize("name", ["c64_og1", "c128_g2_og4_dil2"])

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import TOL, golden_cases, load_golden, rel_err, to_np
+from _util import TOL, golden_cases, load_golden, assert_close, rel_err, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -48,19 +48,19 @@ def test_abi_forward_backward_vs_oracle(name, dtype, cuda):
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
                                                 st, pd, dl, T["mask"], T["bias"] is not None)
     tol = TOL[dtype]
-    assert rel_err(to_np(out), ref_out) <= tol
-    assert rel_err(to_np(gi), rgi) <= tol
-    assert rel_err(to_np(goff), rgoff) <= tol
-    assert rel_err(to_np(gw), rgw) <= tol
+    assert_close(out, ref_out, dtype, 'out')
+    assert_close(gi, rgi, dtype, 'gi')
+    assert_close(goff, rgoff, dtype, 'goff')
+    assert_close(gw, rgw, dtype, 'gw')
     if T["bias"] is not None:
-        assert rel_err(to_np(gb), rgb) <= tol
+        assert_close(gb, rgb, dtype, 'gb')
     if T["mask"] is not None:
-        assert rel_err(to_np(gm), rgm) <= tol
+        assert_close(gm, rgm, dtype, 'gm')
     if dtype == "float32":  # and directly against the torchvision fixtures
-        assert rel_err(to_np(out), d["output"]) <= tol
-        assert rel_err(to_np(gi), d["grad_input"]) <= tol
-        assert rel_err(to_np(goff), d["grad_offset"]) <= tol
-        assert rel_err(to_np(gw), d["grad_weight"]) <= tol
+        assert_close(out, d["output"], dtype, 'out')
+        assert_close(gi, d["grad_input"], dtype, 'gi')
+        assert_close(goff, d["grad_offset"], dtype, 'goff')
+        assert_close(gw, d["grad_weight"], dtype, 'gw')
 
 
 @pytest.mark.parametrize("dtype", list(DTYPES))
@@ -80,14 +80,14 @@ def test_python_api_autograd_vs_oracle(name, dtype, cuda):
                                                 st, pd, dl, T["mask"], T["bias"] is not None)
     tol = TOL[dtype]
     assert out.dtype == DTYPES[dtype] and out.is_cuda
-    assert rel_err(to_np(out), ref_out) <= tol
-    assert rel_err(to_np(leaves["input"].grad), rgi) <= tol
-    assert rel_err(to_np(leaves["offset"].grad), rgoff) <= tol
-    assert rel_err(to_np(leaves["weight"].grad), rgw) <= tol
+    assert_close(out, ref_out, dtype, 'out')
+    assert_close(leaves["input"].grad, rgi, dtype, 'leaves["input"].grad')
+    assert_close(leaves["offset"].grad, rgoff, dtype, 'leaves["offset"].grad')
+    assert_close(leaves["weight"].grad, rgw, dtype, 'leaves["weight"].grad')
     if "bias" in leaves:
-        assert rel_err(to_np(leaves["bias"].grad), rgb) <= tol
+        assert_close(leaves["bias"].grad, rgb, dtype, 'leaves["bias"].grad')
     if "mask" in leaves:
-        assert rel_err(to_np(leaves["mask"].grad), rgm) <= tol
+        assert_close(leaves["mask"].grad, rgm, dtype, 'leaves["mask"].grad')
 
 
 @pytest.mark.parametrize("dtype", list(DTYPES))
@@ -105,17 +105,17 @@ def test_reference_column_interface(dtype, cuda):
     cols = lib.deformable_im2col(x, off, m, kh, kw, st[0], st[1], pd[0], pd[1], dl[0], dl[1], og, True)
     rcols = oracle.im2col(x, off, m, kh, kw, st, pd, dl, og)
     assert tuple(cols.shape) == rcols.shape
-    assert rel_err(to_np(cols), rcols) <= TOL[dtype]
+    assert_close(cols, rcols, dtype, 'cols')
     gcol = torch.randn(cols.shape, device=cuda, dtype=torch.float32).to(DTYPES[dtype])
     gi = lib.deform_conv2d_backward_input(gcol, x, off, m, x.shape[2], x.shape[3], st[0], st[1], pd[0],
                                           pd[1], dl[0], dl[1], kh, kw, og, True)
     rgi = oracle.col2im(gcol, tuple(x.shape), off, m, kh, kw, st, pd, dl, og)
-    assert rel_err(to_np(gi), rgi) <= TOL[dtype]
+    assert_close(gi, rgi, dtype, 'gi')
     goff, gm = lib.deform_conv2d_backward_offset_mask(gcol, x, off, m, kh, kw, st[0], st[1], pd[0],
                                                       pd[1], dl[0], dl[1], og, True)
     rgoff, rgm = oracle.col2im_coord(gcol, x, off, m, kh, kw, st, pd, dl, og)
-    assert rel_err(to_np(goff), rgoff) <= TOL[dtype]
-    assert rel_err(to_np(gm), rgm) <= TOL[dtype]
+    assert_close(goff, rgoff, dtype, 'goff')
+    assert_close(gm, rgm, dtype, 'gm')
 
 
 def test_empty_batch(cuda):
@@ -153,7 +153,7 @@ def test_simt_forward_k_split_vs_oracle(shape, cuda):
     torch.cuda.synchronize()
     assert torch.equal(a, a2)
     ref = oracle.forward(x, off, w, b, (1, 1), (1, 1), (1, 1), m)
-    assert rel_err(to_np(a), ref) <= TOL["float32"]
+    assert_close(a, ref, "float32", 'a')
 
 
 def test_device_status_clean_after_runs(cuda):

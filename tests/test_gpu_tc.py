@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import TOL, rel_err, to_np
+from _util import TOL, assert_close, rel_err, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -61,10 +61,10 @@ def test_tc_forward_vs_oracle(name, dtype, cuda):
     torch.cuda.synchronize()
     lib.device_status()
     ref = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
-    assert rel_err(to_np(out), ref) <= TOL[dtype]
+    assert_close(out, ref, dtype, 'out')
     # and through the public autograd API
     out2 = mdc.deform_conv2d(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
-    assert rel_err(to_np(out2), ref) <= TOL[dtype]
+    assert_close(out2, ref, dtype, 'out2')
 
 
 @pytest.mark.parametrize("dtype", list(DTYPES))
@@ -79,13 +79,13 @@ def test_tc_backward_vs_oracle(name, dtype, cuda):
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
                                                 st, pd, dl, T["mask"], T["bias"] is not None)
     tol = TOL[dtype]
-    assert rel_err(to_np(gi), rgi) <= tol
-    assert rel_err(to_np(goff), rgoff) <= tol
-    assert rel_err(to_np(gw), rgw) <= tol
+    assert_close(gi, rgi, dtype, 'gi')
+    assert_close(goff, rgoff, dtype, 'goff')
+    assert_close(gw, rgw, dtype, 'gw')
     if T["bias"] is not None:
-        assert rel_err(to_np(gb), rgb) <= tol
+        assert_close(gb, rgb, dtype, 'gb')
     if T["mask"] is not None:
-        assert rel_err(to_np(gm), rgm) <= tol
+        assert_close(gm, rgm, dtype, 'gm')
 
 
 def test_tc_forward_deterministic_and_batch_consistent(cuda):
@@ -132,7 +132,7 @@ def test_tc_layout_passes_unaligned_pointers(dtype, cuda):
     for name, p, q in zip(("input", "offset", "weight", "bias", "mask"), ga, gu):
         assert rel_err(to_np(q), to_np(p)) <= 1e-3, name
     ref = oracle.forward(T["input"], T["offset"], T["weight"], T["bias"], st, pd, dl, T["mask"])
-    assert rel_err(to_np(u), ref) <= TOL[dtype]
+    assert_close(u, ref, dtype, 'u')
 
 
 @pytest.mark.parametrize("mask_sel", [(1, 0, 0, 0, 0), (0, 1, 0, 0, 1), (0, 0, 1, 1, 0)])
@@ -176,14 +176,14 @@ def test_tc_autograd_training_cache(name, cache, cuda):
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(T["grad_output"], T["input"], T["offset"], T["weight"],
                                                 st, pd, dl, T["mask"], T["bias"] is not None)
     tol = TOL["bfloat16"]
-    assert rel_err(to_np(out), ref_out) <= tol
-    assert rel_err(to_np(leaves["input"].grad), rgi) <= tol
-    assert rel_err(to_np(leaves["offset"].grad), rgoff) <= tol
-    assert rel_err(to_np(leaves["weight"].grad), rgw) <= tol
+    assert_close(out, ref_out, "bfloat16", 'out')
+    assert_close(leaves["input"].grad, rgi, "bfloat16", 'leaves["input"].grad')
+    assert_close(leaves["offset"].grad, rgoff, "bfloat16", 'leaves["offset"].grad')
+    assert_close(leaves["weight"].grad, rgw, "bfloat16", 'leaves["weight"].grad')
     if "bias" in leaves:
-        assert rel_err(to_np(leaves["bias"].grad), rgb) <= tol
+        assert_close(leaves["bias"].grad, rgb, "bfloat16", 'leaves["bias"].grad')
     if "mask" in leaves:
-        assert rel_err(to_np(leaves["mask"].grad), rgm) <= tol
+        assert_close(leaves["mask"].grad, rgm, "bfloat16", 'leaves["mask"].grad')
 
 
 @pytest.mark.parametrize("cache", [True, False])
@@ -210,7 +210,7 @@ def test_tc_weight_grad_deterministic(cache, cuda):
     _, _, rgw, _, _ = oracle.backward(T["grad_output"][:2], T["input"][:2], T["offset"][:2], T["weight"], st, pd,
                                       dl, T["mask"][:2], False)
     assert torch.isfinite(gw[0]).all()
-    assert rel_err(to_np(gw[0]) / 16.0, rgw) <= TOL["bfloat16"]
+    assert_close(to_np(gw[0]) / 16.0, rgw, "bfloat16", "grad_weight / 16")
 
 
 def test_abi_training_pair_matches_plain_calls(cuda):

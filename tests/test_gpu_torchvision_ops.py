@@ -5,7 +5,7 @@ float64 oracle, and proof that the library's kernels ran (launch count)."""
 import pytest
 import torch
 
-from _util import TOL, rel_err, to_np
+from _util import TOL, assert_close, rel_err, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -34,13 +34,13 @@ def test_torchvision_deform_conv2d_runs_on_b200_kernels(dtype, C, mask, cuda):
     out.backward(GO)
     torch.cuda.synchronize()
     assert _abi.launch_count() > n0  # this library's kernels served the call
-    tol = TOL[{torch.float32: "float32", torch.float16: "float16", torch.bfloat16: "bfloat16"}[dtype]]
+    DTN = {torch.float32: "float32", torch.float16: "float16", torch.bfloat16: "bfloat16"}[dtype]
     ref = oracle.forward(X, OFF, Wt, Bt, 1, 1, 1, M)
     rgi, rgoff, rgw, rgb, rgm = oracle.backward(GO, X, OFF, Wt, 1, 1, 1, M, True)
-    assert rel_err(to_np(out), ref) <= tol
-    assert rel_err(to_np(leaves[0].grad), rgi) <= tol
-    assert rel_err(to_np(leaves[1].grad), rgoff) <= tol
-    assert rel_err(to_np(leaves[2].grad), rgw) <= tol
-    assert rel_err(to_np(leaves[3].grad), rgb) <= tol
+    assert_close(out, ref, DTN, 'out')
+    assert_close(leaves[0].grad, rgi, DTN, 'leaves[0].grad')
+    assert_close(leaves[1].grad, rgoff, DTN, 'leaves[1].grad')
+    assert_close(leaves[2].grad, rgw, DTN, 'leaves[2].grad')
+    assert_close(leaves[3].grad, rgb, DTN, 'leaves[3].grad')
     if mask:
-        assert rel_err(to_np(leaves[4].grad), rgm) <= tol
+        assert_close(leaves[4].grad, rgm, DTN, 'leaves[4].grad')

@@ -36,6 +36,18 @@ def test_oracle_backward_matches_torchvision(name):
         np.testing.assert_allclose(gm, d["grad_mask"], rtol=1e-12, atol=1e-12)
 
 
+@pytest.mark.parametrize("name", [c for c in CASES if c != "empty_batch"])
+def test_oracle_param_grads_match_torchvision(name):
+    """The BLAS-product path for large shards (oracle.param_grads) gives the
+    torchvision grad_weight / grad_bias of every fixture."""
+    d = load_golden(name)
+    gw, gb = oracle.param_grads(d["grad_output"], d["input"], d["offset"], d["weight"], tuple(d["stride"]),
+                                tuple(d["padding"]), tuple(d["dilation"]), d.get("mask"))
+    np.testing.assert_allclose(gw, d["grad_weight"], rtol=1e-11, atol=1e-12)
+    if "bias" in d:
+        np.testing.assert_allclose(gb, d["grad_bias"], rtol=1e-12, atol=1e-12)
+
+
 @pytest.mark.parametrize("name", ["mask_bias_g2_og2", "stride2_dil2", "integer_offsets"])
 def test_oracle_column_pieces_compose(name):
     """im2col / col2im / col2im_coord compose to the same gradients (groups=1 slice)."""
