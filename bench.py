@@ -17,6 +17,7 @@ bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -226,6 +227,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     p = PROBLEMS[args.workload]
+    if args.batch:  # a reduced case of the same layer (ncu captures); the JSON line names its batch
+        p = dataclasses.replace(p, batch=args.batch)
     first, nb = shard_range(p.batch, world, rank)
     peaks = load_peaks()
     inp = make_inputs(p, dev, batch=nb, batch_offset=first)
@@ -612,6 +615,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of a CUDA graph")
     ap.add_argument("--overlap", action="store_true",
                     help="start the parameter-gradient all-reduce from the backward's hook on a side stream")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="global batch override: a reduced case of the workload for ncu captures")
     ap.add_argument("--traffic-per-launch", type=float, default=None,
                     help="ncu dram bytes per launch of the dominant kernel, if captured")
     args = ap.parse_args()

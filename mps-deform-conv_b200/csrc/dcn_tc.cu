@@ -9,8 +9,11 @@
 // exists in memory.
 //
 // Warp roles (576 threads):
-//   warps 0-15  gather producers (gather_run, dcn_tc_common.cuh): 8 lanes per
-//               pixel row, one 16-byte channel vector each, two rows per lane;
+//   warps 0-15  gather producers (dcn_tc_common.cuh): gather_run_wide when
+//               the offset groups span whole 64-channel chunks (4 lanes per
+//               pixel row, 32 bytes of channels each, one sample per lane),
+//               else gather_run (8 lanes per row, 16 bytes each, two rows per
+//               lane);
 //               they read the offset/mask of the (pixel, tap, offset group),
 //               load the 4 bilinear corners from the channels-last input,
 //               blend them with packed 16-bit FMAs and write the
@@ -86,8 +89,9 @@ struct FwdArgs {
   uint32_t tmem_cols;
 };
 
-// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout)
-template <typename T, bool LOGIT>
+// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout); WIDE: the
+// offset groups span whole 64-channel chunks (gather_run_wide)
+template <typename T, bool LOGIT, bool WIDE>
 __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -133,16 +137,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
 
   if (warp < NPROD_WARPS) {
     // ------------------------------------------------ producers
-    const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
-    const PixelCtx pc[2] = {pixel_ctx(g, (long long)tile * BM + r0), pixel_ctx(g, (long long)tile * BM + r0 + 4)};
     Ring ring{0, S, 0u};
-    const bool ok = gather_run<T, LOGIT>(
-        g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status, ST_PROD,
-        [&](int s, uint8_t*& t, uint32_t& eb, uint32_t& fb) {
-          t = smem + L.a + s * A_STAGE_BYTES;  // saved as a column tile by the store lane (training)
-          eb = empty(s);
-          fb = a_full(s);
-        });
+    auto stage_of = [&](int s, uint8_t*& t, uint32_t& eb, uint32_t& fb) {
+      t = smem + L.a + s * A_STAGE_BYTES;  // saved as a column tile by the store lane (training)
+      eb = empty(s);
+      fb = a_full(s);
+    };
+    bool ok;
+    if (WIDE) {
+      const int r = warp * 8 + (lane >> 2);
+      const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
+      ok = gather_run_wide<T, LOGIT>(g, xh, off, msk, pc, r, lane & 3, grp * g.Cig, 0, a.nkc, ring, abort_flag,
+                                     a.status, ST_PROD, stage_of);
+    } else {
+      const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
+      const PixelCtx pc[2] = {pixel_ctx(g, (long long)tile * BM + r0), pixel_ctx(g, (long long)tile * BM + r0 + 4)};
+      ok = gather_run<T, LOGIT>(g, xh, off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc, ring, abort_flag, a.status,
+                                ST_PROD, stage_of);
+    }
     // ------------------------------------------------ epilogue
     // (warp-uniform decision: tcgen05.ld is a .sync.aligned warp instruction)
     const bool acc_ready = ok && mbar_wait(acc_full, 0, abort_flag, a.status, ST_EPI);
@@ -468,7 +480,9 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   a.tmem_cols = tmem_cols_for(g.Cog);
   const FwdSmem SL = fwd_smem_layout(g.Cog, a.stages);
   const int smem = (int)SL.total + 1024;
-  auto kern = g.msk_logit ? dcn_fwd_tc_kernel<T, true> : dcn_fwd_tc_kernel<T, false>;
+  const bool wide = g.cpo % BK == 0;  // one sample per row of every K chunk: gather_run_wide
+  auto kern = g.msk_logit ? (wide ? dcn_fwd_tc_kernel<T, true, true> : dcn_fwd_tc_kernel<T, true, false>)
+                          : (wide ? dcn_fwd_tc_kernel<T, false, true> : dcn_fwd_tc_kernel<T, false, false>);
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
     return e;
   dim3 grid((unsigned)((g.P + BM - 1) / BM), (unsigned)g.G);

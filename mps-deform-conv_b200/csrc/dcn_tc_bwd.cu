@@ -512,7 +512,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
     for (int s = 0; s < S; ++s) { mbar_init(b_full(s), 1); mbar_init(b_empty(s), 1); }
-    for (int e = 0; e < D_NBUF; ++e) { mbar_init(d_full(e), 1); mbar_init(d_empty(e), 128); }
+    for (int e = 0; e < D_NBUF; ++e) { mbar_init(d_full(e), 1); mbar_init(d_empty(e), 4); }  // one per warp
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -579,7 +579,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           }
         }
         tc_fence_before();
-        mbar_arrive(d_empty(e));  // TMEM buffer read completely
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty(e));  // TMEM buffer read completely
       }
       const int o = cbase / g.cpo;  // one offset group per chunk
       float tab_m;
@@ -733,7 +734,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           tmem_ld_wait();
           if (sl == 1) {  // last read of this TMEM buffer: let the MMA reuse it
             tc_fence_before();
-            mbar_arrive(d_empty(e));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty(e));
           }
           float* srow = ws->slab[lane];
 #pragma unroll
@@ -885,7 +887,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         tmem_ld_wait();
         if (sl == 3) {  // last read of this TMEM buffer: let the MMA reuse it
           tc_fence_before();
-          mbar_arrive(d_empty(e));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d_empty(e));
         }
         float* srow = ws->slab[lane];
 #pragma unroll

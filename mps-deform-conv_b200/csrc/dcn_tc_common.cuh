@@ -294,6 +294,113 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
   return true;
 }
 
+// Producer for problems whose offset groups span whole 64-channel chunks
+// (channels per offset group a multiple of 64), where every row of a K chunk
+// has one sample.  Lane l of a producer warp works on row r = 8*warp + l/4
+// and on channels [8q, 8q+8) and [32+8q, 32+8q+8) of the chunk (q = l%4), so
+// one load instruction covers 8 rows x 64 contiguous bytes of a corner and
+// each lane computes one sampling point per new (tap, offset group) -- half
+// the sample arithmetic of gather_run's two pixels per lane, for the same
+// 8 corner loads in flight per lane.  The offsets and mask of the next new
+// sample are loaded one chunk ahead.  Same stage protocol and return value as
+// gather_run; the A tiles are bitwise those of gather_run.  (Issuing chunk
+// i+1's corner loads before chunk i's blend needs about 140 registers per
+// thread, above the 96 that 18 warps per CTA leave.)
+template <typename T, bool LOGIT, class StageFn>
+__device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restrict__ xh,
+                                                const T* __restrict__ off, const T* __restrict__ msk,
+                                                const PixelCtx& pc, int r, int q, int cbase_grp, int kc0, int nk,
+                                                Ring& ring, volatile int* abort_flag, int* status, int code,
+                                                StageFn&& stage_of) {
+  const int ncc = g.Cig / BK;
+  const int cpc = g.cpo / BK;  // consecutive channel chunks per offset group
+  const int xo = (int)pc.img * g.C;
+  const int oo = pc.b * (int)g.off_bs + pc.p, mo = pc.b * (int)g.msk_bs + pc.p;
+  const int og0 = cbase_grp / g.cpo;  // offset group of the weight group's first channel chunk
+  auto load = [&](int o, int t) {
+    RawSample<T> rs;
+    const int ob = oo + (o * 2 * g.T + 2 * t) * g.HWo;
+    rs.dy = off[ob];
+    rs.dx = off[ob + g.HWo];
+    rs.m = msk ? msk[mo + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    return rs;
+  };
+  // chunk position in gather order: tap t = (ti, tj), channel chunk cc, its
+  // offset group o and the chunk's index within that offset group (oc)
+  struct Pos {
+    int t, ti, tj, cc, o, oc;
+  };
+  Pos p0;
+  p0.t = kc0 / ncc;
+  p0.cc = kc0 - p0.t * ncc;
+  p0.ti = p0.t / g.kw;
+  p0.tj = p0.t - p0.ti * g.kw;
+  p0.o = og0 + p0.cc / cpc;
+  p0.oc = p0.cc - (p0.cc / cpc) * cpc;
+  auto advance = [&](Pos p) {
+    if (++p.cc == ncc) {
+      p.cc = 0;
+      p.o = og0;
+      p.oc = 0;
+      ++p.t;
+      if (++p.tj == g.kw) { p.tj = 0; ++p.ti; }
+    } else if (++p.oc == cpc) {
+      p.oc = 0;
+      ++p.o;
+    }
+    return p;
+  };
+  auto issue = [&](const CornerSet32& c, int cc, uint4 (&dst)[8]) {
+    const int cb = cbase_grp + cc * BK + q * 8;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (c.w[k] != 0.f) {
+        const uint4* src = reinterpret_cast<const uint4*>(xh + (uint32_t)(xo + c.off[k] + cb));
+        dst[2 * k] = __ldg(src);
+        dst[2 * k + 1] = __ldg(src + 4);  // 32 channels further
+      } else {
+        dst[2 * k] = make_uint4(0, 0, 0, 0);
+        dst[2 * k + 1] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  CornerSet32 cs = corner_set32<T, LOGIT>(g, pc, load(p0.o, p0.t), p0.ti, p0.tj);
+  uint4 v[8];
+  issue(cs, p0.cc, v);
+  Pos p1 = p0;
+  RawSample<T> raw1{};
+  if (nk > 1) {
+    p1 = advance(p0);
+    if (p1.t != p0.t || p1.o != p0.o) raw1 = load(p1.o, p1.t);
+  }
+  const int o_lo = r * 128 + ((q ^ (r & 7)) << 4), o_hi = r * 128 + (((q + 4) ^ (r & 7)) << 4);
+  for (int i = 0; i < nk; ++i) {
+    const uint4 c_lo[4] = {v[0], v[2], v[4], v[6]}, c_hi[4] = {v[1], v[3], v[5], v[7]};
+    const uint4 b_lo = blend8<T>(c_lo, cs.w), b_hi = blend8<T>(c_hi, cs.w);
+    uint8_t* tile;
+    uint32_t empty_bar, full_bar;
+    stage_of(ring.s, tile, empty_bar, full_bar);
+    if (!mbar_wait(empty_bar, ring.ph ^ 1u, abort_flag, status, code)) return false;
+    *reinterpret_cast<uint4*>(tile + o_lo) = b_lo;
+    *reinterpret_cast<uint4*>(tile + o_hi) = b_hi;
+    fence_async_shared();
+    mbar_arrive(full_bar);
+    ring.next();
+    if (i + 1 < nk) {
+      // chunk i+1: a new sampling point only when the tap or offset group
+      // changes; then the offsets and mask of the chunk after it
+      if (p1.t != p0.t || p1.o != p0.o) cs = corner_set32<T, LOGIT>(g, pc, raw1, p1.ti, p1.tj);
+      issue(cs, p1.cc, v);
+      p0 = p1;
+      if (i + 2 < nk) {
+        p1 = advance(p0);
+        if (p1.t != p0.t || p1.o != p0.o) raw1 = load(p1.o, p1.t);
+      }
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- TMA (tensor)
 // 2-D tiled load (no multicast): box at (x = inner coordinate, y) of the
 // tensor described by `tmap` into shared memory at `dst`, completing as
