@@ -9,10 +9,12 @@
 // exists in memory.
 //
 // Warp roles (576 threads):
-//   warps 0-15  gather producers (dcn_tc_common.cuh): gather_run_wide when
-//               the offset groups span whole 64-channel chunks (4 lanes per
-//               pixel row, 32 bytes of channels each, one sample per lane),
-//               else gather_run (8 lanes per row, 16 bytes each, two rows per
+//   warps 0-15  gather producers (dcn_tc_common.cuh): gather_run_quad for
+//               offset groups of 8 channels (each sample's four corners from
+//               one 64-byte corner-quad record), gather_run_wide when offset
+//               groups span whole 64-channel chunks (4 lanes per pixel row,
+//               32 bytes of channels each, one sample per lane), else
+//               gather_run (8 lanes per row, 16 bytes each, two rows per
 //               lane);
 //               they read the offset/mask of the (pixel, tap, offset group),
 //               load the 4 bilinear corners from the channels-last input,
@@ -79,6 +81,7 @@ struct FwdArgs {
   const void* bias;   // [Co] or null
   void* out;          // [B][Co][Ho][Wo]
   const void* wsw;    // weights, pre-swizzled [G][NKC][Cog][64]
+  const void* xq;     // corner-quad records (offset groups of 8 channels), or null
   void* cols;         // copy of every A tile [G][n_tiles][NKC][16 KB], or null
   int* status;
   Geom g;
@@ -89,9 +92,14 @@ struct FwdArgs {
   uint32_t tmem_cols;
 };
 
-// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout); WIDE: the
-// offset groups span whole 64-channel chunks (gather_run_wide)
-template <typename T, bool LOGIT, bool WIDE>
+// Gather producers (dcn_tc_common.cuh).
+constexpr int PROD_GENERAL = 0;  // gather_run: any offset groups of a multiple of 8 channels
+constexpr int PROD_WIDE = 1;     // gather_run_wide: offset groups span whole 64-channel chunks
+constexpr int PROD_QUAD = 2;     // gather_run_quad: offset groups of 8 channels, corner-quad records
+
+// LOGIT = a.g.msk_logit (mask logits of the DCNv2 head layout); PROD: the
+// gather producer (above)
+template <typename T, bool LOGIT, int PROD>
 __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -144,7 +152,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) dcn_fwd_tc_kernel(const FwdArgs a
       fb = a_full(s);
     };
     bool ok;
-    if (WIDE) {
+    if (PROD == PROD_QUAD) {
+      const int r0 = warp * 8 + (lane >> 3), q = lane & 7;
+      const PixelCtx pc[2] = {pixel_ctx(g, (long long)tile * BM + r0), pixel_ctx(g, (long long)tile * BM + r0 + 4)};
+      ok = gather_run_quad<T, LOGIT>(g, static_cast<const T*>(a.xq), off, msk, pc, r0, q, grp * g.Cig, 0, a.nkc,
+                                     ring, abort_flag, a.status, ST_PROD, stage_of);
+    } else if (PROD == PROD_WIDE) {
       const int r = warp * 8 + (lane >> 2);
       const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + r);
       ok = gather_run_wide<T, LOGIT>(g, xh, off, msk, pc, r, lane & 3, grp * g.Cig, 0, a.nkc, ring, abort_flag,
@@ -291,6 +304,31 @@ __global__ void nchw_to_nhwc_kernel(const T* __restrict__ x, T* __restrict__ xh,
   }
 }
 
+// channels-last input [B][H][W][C] -> corner-quad records (gather_run_quad):
+// one thread per (record, corner) copies 16 bytes (offset group o's 8
+// channels of one corner, zero outside the image).  Consecutive threads write
+// consecutive 16 bytes and read whole 128-byte pixel rows.
+template <typename T>
+__global__ void quad_records_kernel(const T* __restrict__ xh, T* __restrict__ xq, int H, int W, int C,
+                                    long long n) {
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const int k = (int)(t & 3);
+  const int og8 = C / 8;
+  const long long rec = t >> 2;
+  const int o = (int)(rec % og8);
+  const long long pix = rec / og8;  // ((b*(H+1) + y0+1)*(W+1) + x0+1)
+  const int xx = (int)(pix % (W + 1));
+  const long long by = pix / (W + 1);
+  const int yy = (int)(by % (H + 1));
+  const int b = (int)(by / (H + 1));
+  const int y = yy - 1 + (k >> 1), x = xx - 1 + (k & 1);
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (y >= 0 && y < H && x >= 0 && x < W)
+    v = *reinterpret_cast<const uint4*>(xh + (((long long)b * H + y) * W + x) * C + o * 8);
+  reinterpret_cast<uint4*>(xq)[t] = v;
+}
+
 // weight [Co][Cig][T] -> [G][NKC][Cog][64] in the producers' gather order,
 // K chunk kc = t * (Cig/64) + cc (channel chunk fastest), rows 128-byte
 // swizzled (chunk q of row co at q ^ (co % 8)).
@@ -343,14 +381,19 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
   return true;
 }
 
+// Offset groups of 8 channels gather from corner-quad records (32-bit
+// element offsets).
+static bool use_quad(const Geom& g) { return g.cpo == 8 && quad_elems(g) < (1LL << 31); }
+
 struct FwdWs {
-  size_t xh, wsw, total;
+  size_t xh, wsw, xq, total;
 };
 static FwdWs fwd_ws(const Geom& g, size_t es) {
   FwdWs L;
   L.xh = 0;
   L.wsw = ws_align(es * (size_t)g.B * g.C * g.H * g.W);
-  L.total = L.wsw + ws_align(es * (size_t)g.Co * g.Cig * g.T);
+  L.xq = L.wsw + ws_align(es * (size_t)g.Co * g.Cig * g.T);
+  L.total = L.xq + (use_quad(g) ? ws_align(es * (size_t)quad_elems(g)) : 0);
   return L;
 }
 
@@ -468,8 +511,18 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
+  const bool quad = use_quad(g) && (reinterpret_cast<uintptr_t>(xh) & 15) == 0;
+  T* xq = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.xq);
+  if (quad) {
+    KernelScope ks("quad_records", st);
+    const long long n = quad_elems(g) / 8;  // 16-byte pieces
+    quad_records_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xh, xq, g.H, g.W, g.C, n);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+
   FwdArgs a;
   a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.bias = bias; a.out = out; a.wsw = wsw;
+  a.xq = quad ? xq : nullptr;
   a.cols = saved ? static_cast<char*>(saved) + SV.cols : nullptr;
   if ((e = tc_status_ptr(&a.status)) != cudaSuccess) return e;
   a.g = g;
@@ -480,9 +533,15 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   a.tmem_cols = tmem_cols_for(g.Cog);
   const FwdSmem SL = fwd_smem_layout(g.Cog, a.stages);
   const int smem = (int)SL.total + 1024;
-  const bool wide = g.cpo % BK == 0;  // one sample per row of every K chunk: gather_run_wide
-  auto kern = g.msk_logit ? (wide ? dcn_fwd_tc_kernel<T, true, true> : dcn_fwd_tc_kernel<T, true, false>)
-                          : (wide ? dcn_fwd_tc_kernel<T, false, true> : dcn_fwd_tc_kernel<T, false, false>);
+  // producer: corner-quad records for offset groups of 8 channels, one
+  // sample per lane when offset groups span whole 64-channel chunks, else
+  // the general two-rows-per-lane gather
+  const int prod = quad ? PROD_QUAD : g.cpo % BK == 0 ? PROD_WIDE : PROD_GENERAL;
+  auto pick = [&](auto k0, auto k1, auto k2) { return prod == PROD_QUAD ? k2 : prod == PROD_WIDE ? k1 : k0; };
+  auto kern = g.msk_logit ? pick(dcn_fwd_tc_kernel<T, true, PROD_GENERAL>, dcn_fwd_tc_kernel<T, true, PROD_WIDE>,
+                                 dcn_fwd_tc_kernel<T, true, PROD_QUAD>)
+                          : pick(dcn_fwd_tc_kernel<T, false, PROD_GENERAL>, dcn_fwd_tc_kernel<T, false, PROD_WIDE>,
+                                 dcn_fwd_tc_kernel<T, false, PROD_QUAD>);
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
     return e;
   dim3 grid((unsigned)((g.P + BM - 1) / BM), (unsigned)g.G);

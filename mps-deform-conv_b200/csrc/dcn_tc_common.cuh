@@ -40,6 +40,14 @@ template <> struct Vec<__half> {
   }
 };
 
+// 32 bytes of read-only global memory in one 256-bit load (sm_100);
+// p 32-byte aligned.
+__device__ __forceinline__ void ldg256(const void* p, uint4& lo, uint4& hi) {
+  asm("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+      : "l"(p));
+}
+
 // ---------------------------------------------------------------- gather
 // A producer warp owns 8 consecutive pixel rows (8*warp .. 8*warp+7) of a
 // 128-row operand tile [pixels][64 channels] (lane mapping: gather_run).
@@ -350,6 +358,8 @@ __device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restri
     }
     return p;
   };
+  // the lane's channels [8q, 8q+8) and [32+8q, 32+8q+8): two 128-bit loads
+  // per corner (one 256-bit load of [16q, 16q+16) measured no faster)
   auto issue = [&](const CornerSet32& c, int cc, uint4 (&dst)[8]) {
     const int cb = cbase_grp + cc * BK + q * 8;
 #pragma unroll
@@ -397,6 +407,91 @@ __device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restri
         if (p1.t != p0.t || p1.o != p0.o) raw1 = load(p1.o, p1.t);
       }
     }
+  }
+  return true;
+}
+
+// Corner-quad records for offset groups of 8 channels.  Record (b, y0, x0, o)
+// holds the 8 channels of offset group o at the four corners (y0, x0),
+// (y0, x0+1), (y0+1, x0), (y0+1, x0+1) of image b, corner-major, 64 bytes;
+// corners outside the image are zero.  y0 runs over [-1, H-1] and x0 over
+// [-1, W-1], so every sample inside (-1, H) x (-1, W) has its record, and
+// one record replaces the sample's four scattered 16-byte corner reads.
+// Element offset of a record: ((b*(H+1) + y0+1)*(W+1) + x0+1)*C*4 + o*32.
+__host__ __device__ inline long long quad_elems(const Geom& g) {
+  return (long long)g.B * (g.H + 1) * (g.W + 1) * g.C * 4;
+}
+
+// Producer for offset groups of exactly 8 channels (one group per lane's
+// 16-byte channel vector): lanes and rows as gather_run, each sample read from
+// its corner-quad record with two 256-bit loads.  Same stage protocol and
+// return value as gather_run.
+template <typename T, bool LOGIT, class StageFn>
+__device__ __forceinline__ bool gather_run_quad(const Geom& g, const T* __restrict__ xq,
+                                                const T* __restrict__ off, const T* __restrict__ msk,
+                                                const PixelCtx (&pc)[2], int r0, int q, int cbase_grp, int kc0,
+                                                int nk, Ring& ring, volatile int* abort_flag, int* status, int code,
+                                                StageFn&& stage_of) {
+  const int ncc = g.Cig / BK;
+  int qb[2], oo[2], mo[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    qb[h] = pc[h].b * (g.H + 1);  // record row of (b, y0 = -1)
+    oo[h] = pc[h].b * (int)g.off_bs + pc[h].p;
+    mo[h] = pc[h].b * (int)g.msk_bs + pc[h].p;
+  }
+  auto load = [&](int h, int o, int t) {
+    RawSample<T> rs;
+    const int ob = oo[h] + (o * 2 * g.T + 2 * t) * g.HWo;
+    rs.dy = off[ob];
+    rs.dx = off[ob + g.HWo];
+    rs.m = msk ? msk[mo[h] + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    return rs;
+  };
+  GatherWalk kw;
+  kw.start(g, kc0, ncc);
+  int o = (cbase_grp + kw.cc * BK) / 8 + q;  // the lane's offset group (8 channels each)
+  RawSample<T> raw[2] = {load(0, o, kw.t), load(1, o, kw.t)};
+  const int r1 = r0 + 4;
+  const int o0 = r0 * 128 + ((q ^ (r0 & 7)) << 4), o1 = r1 * 128 + ((q ^ (r1 & 7)) << 4);
+  for (int i = 0; i < nk; ++i) {
+    uint4 v[2][4];
+    float w[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const SamplePos sp = sample_pos(pc[h].y0 + kw.ti * g.dh, pc[h].x0 + kw.tj * g.dw, to_f(raw[h].dy),
+                                      to_f(raw[h].dx));
+      const Corners c = corners_of(sp, g.H, g.W);
+      const float mv = to_f(raw[h].m);
+      const float m = pc[h].valid ? (LOGIT ? 1.f / (1.f + __expf(-mv)) : mv) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[h][k] = c.w[k] * m;
+      // a non-zero weight implies the sample lies inside (-1, H) x (-1, W)
+      if (w[h][0] != 0.f || w[h][1] != 0.f || w[h][2] != 0.f || w[h][3] != 0.f) {
+        const T* rec = xq + (uint32_t)(((qb[h] + sp.y0 + 1) * (g.W + 1) + sp.x0 + 1) * (g.C * 4) + o * 32);
+        ldg256(rec, v[h][0], v[h][1]);
+        ldg256(rec + 16, v[h][2], v[h][3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[h][k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (i + 1 < nk) {  // the next chunk's offsets and mask
+      kw.next(g, ncc);
+      o = (cbase_grp + kw.cc * BK) / 8 + q;
+      raw[0] = load(0, o, kw.t);
+      raw[1] = load(1, o, kw.t);
+    }
+    uint8_t* tile;
+    uint32_t empty_bar, full_bar;
+    stage_of(ring.s, tile, empty_bar, full_bar);
+    const uint4 b0 = blend8<T>(v[0], w[0]), b1 = blend8<T>(v[1], w[1]);
+    if (!mbar_wait(empty_bar, ring.ph ^ 1u, abort_flag, status, code)) return false;
+    *reinterpret_cast<uint4*>(tile + o0) = b0;
+    *reinterpret_cast<uint4*>(tile + o1) = b1;
+    fence_async_shared();
+    mbar_arrive(full_bar);
+    ring.next();
   }
   return true;
 }
