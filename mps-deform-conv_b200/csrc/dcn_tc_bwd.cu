@@ -411,6 +411,8 @@ struct DgradArgs {
   float* gi32;       // channels-last [B][H][W][C], zeroed
   float* goff32;     // [B][OG*2T][HWo], zeroed
   float* gmsk32;     // [B][OG*T][HWo], zeroed (null without mask)
+  const void* xq;    // quad epilogue (SW = 8): corner-quad records of the input
+  float* gq32;       // quad epilogue: fp32 corner-quad accumulator, zeroed (null: no grad_input)
   int* status;
   Geom g;
   int nkc;           // K chunks per group, kc = cc*T + t
@@ -453,6 +455,19 @@ struct DgWarpSmem64 {
   uint32_t tab[32][12];
 };
 
+// Per-warp epilogue scratch of the quad variant (offset groups of 8
+// channels): the chunk's gcol rows as 16-bit pairs (as DgWarpSmem64), the
+// warp's 32 pixels (image or -1, pixel, y and x base), and a staging area
+// where each lane leaves its sample's 32 fp32 contributions (a corner-quad
+// record, corner-major) and the record's index (-1: none) so that each
+// reduction instruction can cover four whole records.
+struct DgWarpSmemQ {
+  uint32_t slab[32][32];
+  int4 pix[32];
+  float stage[32][32];
+  int rec[32];
+};
+
 // Shared memory: the whole gOt tile [128 px][KB*64 co] stays resident; W^T
 // streams through b_stages stages of one 8 KB K block ([64 ch][64 co]) each;
 // then the epilogue warps' scratch.
@@ -467,6 +482,7 @@ __host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages, int sw) {
   L.epi = L.b + b_stages * L.b_stage;
   L.bar = L.epi + D_EPI_WARPS * (uint32_t)(sw == 64   ? sizeof(DgWarpSmem64)
                                             : sw == 32 ? sizeof(DgWarpSmem32)
+                                            : sw == 8  ? sizeof(DgWarpSmemQ)
                                                        : sizeof(DgWarpSmem));
   L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
   return L;
@@ -482,7 +498,12 @@ __device__ __forceinline__ void red_v4(float* p, float a, float b, float c, floa
 // 16-bit pairs, 16-byte corner loads); 32 when they are a multiple of 32
 // channels (8 lanes x 4 channels per pixel: each corner's 32 fp32 gradients
 // are one 128-byte line, half the lines per byte of SW = 16; 32-bit element
-// offsets); else 16 (4 lanes x 4 channels, up to 2 offset groups per slab).
+// offsets); 8 for offset groups of exactly 8 channels with 32-bit corner-quad
+// offsets (one lane per (pixel, offset group): the sample's four corners
+// from one corner-quad record, its offset and mask gradients complete in the
+// lane, and its 32 contributions added to an fp32 corner-quad accumulator
+// as one 128-byte line); else 16 (4 lanes x 4 channels, up to 2 offset
+// groups per slab).
 template <typename T, int SW>
 __global__ void __launch_bounds__(D_NTHREADS, 1)
 dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_go) {
@@ -680,6 +701,154 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         }
       }
       __syncwarp();  // the next chunk's phase 1 rewrites the rows
+    }
+  } else if (warp < D_EPI_WARPS && SW == 8) {
+    // -------------------------------------------- epilogue, corner-quad (offset groups of 8 channels)
+    //  (1) row owner (lane = TMEM row = pixel): its 64 gcol values to the
+    //      slab as 16-bit pairs; the TMEM buffer is then free;
+    //  (2) lane = (pixel rr, offset group j8 of the chunk), 4 pixels per
+    //      step: the sample from the offsets and mask, the four corners from
+    //      its corner-quad record (two 256-bit loads), the offset and mask
+    //      gradients (all 8 channels of the group are in the lane: plain
+    //      stores, each (pixel, group, tap) is produced once), and the 32
+    //      contributions mask * w_k * gcol_c to the warp's staging area;
+    //      then 8 rounds in which 8 lanes add the 8 16-byte pieces of one
+    //      record with red.global.add.v4.f32, four whole records (128-byte
+    //      lines) per instruction.
+    const T* xq = static_cast<const T*>(a.xq);
+    const T* off = static_cast<const T*>(a.off);
+    const T* msk = static_cast<const T*>(a.msk);
+    const int e = warp >> 2, q = warp & 3;
+    DgWarpSmemQ* ws = reinterpret_cast<DgWarpSmemQ*>(smem + L.epi) + warp;
+    {
+      const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
+      ws->pix[lane] = make_int4(pc.valid ? pc.b : -1, pc.p, pc.y0, pc.x0);
+    }
+    const int j8 = lane & 7, rsub = lane >> 3;
+    const int W1 = g.W + 1, OG = g.C / 8;
+    bool ok = true;
+    for (int i = e; i < nkc_cta; i += D_NBUF) {
+      const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
+      ok = __all_sync(0xffffffffu, ready);
+      if (!ok) break;
+      tc_fence_after();
+      KWalk kw;
+      kw.start(g, kc_lo + i);
+      const int cbase = grp * g.Cig + kw.cc * BK;
+      const int o = cbase / 8 + j8;  // the lane's offset group
+      // ---- phase 1: row owner
+      {
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(e * 64);
+        uint32_t* srow = ws->slab[lane];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t a0[16], a1[16];
+          tmem_ld16(taddr + h * 32, a0);
+          tmem_ld16(taddr + h * 32 + 16, a1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            *reinterpret_cast<uint4*>(srow + (((4 * h + k) ^ (lane & 7)) << 2)) = make_uint4(
+                Vec<T>::pack(__uint_as_float(a0[8 * k]), __uint_as_float(a0[8 * k + 1])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 2]), __uint_as_float(a0[8 * k + 3])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 4]), __uint_as_float(a0[8 * k + 5])),
+                Vec<T>::pack(__uint_as_float(a0[8 * k + 6]), __uint_as_float(a0[8 * k + 7])));
+            *reinterpret_cast<uint4*>(srow + (((4 * h + 2 + k) ^ (lane & 7)) << 2)) = make_uint4(
+                Vec<T>::pack(__uint_as_float(a1[8 * k]), __uint_as_float(a1[8 * k + 1])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 2]), __uint_as_float(a1[8 * k + 3])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 4]), __uint_as_float(a1[8 * k + 5])),
+                Vec<T>::pack(__uint_as_float(a1[8 * k + 6]), __uint_as_float(a1[8 * k + 7])));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty(e));  // TMEM buffer read completely
+      }
+      __syncwarp();
+      // ---- phase 2: lane = (pixel, offset group), 4 pixels per step
+#pragma unroll 1
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + rsub;
+        const int4 px = ws->pix[rr];
+        const uint4 gd = *reinterpret_cast<const uint4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2));
+        float gc[8];
+        {
+          const float2 g01 = Vec<T>::unpack(gd.x), g23 = Vec<T>::unpack(gd.y), g45 = Vec<T>::unpack(gd.z),
+                       g67 = Vec<T>::unpack(gd.w);
+          gc[0] = g01.x; gc[1] = g01.y; gc[2] = g23.x; gc[3] = g23.y;
+          gc[4] = g45.x; gc[5] = g45.y; gc[6] = g67.x; gc[7] = g67.y;
+        }
+        int rec = -1;
+        float wm[4] = {0.f, 0.f, 0.f, 0.f};
+        if (px.x >= 0) {
+          const long long ob = (long long)px.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + px.y;
+          const float dy = to_f(off[ob]), dx = to_f(off[ob + g.HWo]);
+          const float m = g.use_mask ? mask_of(g, to_f(msk[(long long)px.x * g.msk_bs +
+                                                           (long long)(o * g.T + kw.t) * g.HWo + px.y]))
+                                     : 1.f;
+          const SamplePos sp = sample_pos(px.z + kw.ti * g.dh, px.w + kw.tj * g.dw, dy, dx);
+          const Corners cs = corners_of(sp, g.H, g.W);
+          // the record covers every corner of a sample whose floor lies in
+          // [-1, H-1] x [-1, W-1]; other samples have no corner in the image
+          uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                         make_uint4(0, 0, 0, 0)};
+          if (sp.y0 >= -1 && sp.y0 < g.H && sp.x0 >= -1 && sp.x0 < g.W) {
+            rec = ((px.x * (g.H + 1) + sp.y0 + 1) * W1 + sp.x0 + 1) * OG + o;
+            const T* r = xq + (uint32_t)rec * 32u;
+            ldg256(r, xv[0], xv[1]);
+            ldg256(r + 16, xv[2], xv[3]);
+          }
+          float d[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 x01 = Vec<T>::unpack(xv[k].x), x23 = Vec<T>::unpack(xv[k].y),
+                         x45 = Vec<T>::unpack(xv[k].z), x67 = Vec<T>::unpack(xv[k].w);
+            d[k] = gc[0] * x01.x + gc[1] * x01.y + gc[2] * x23.x + gc[3] * x23.y + gc[4] * x45.x + gc[5] * x45.y +
+                   gc[6] * x67.x + gc[7] * x67.y;
+          }
+          // coordinate derivative: corners outside the image hold zeros in the
+          // record, as get_coordinate_weight's per-corner validity does
+          const float gy = m * (sp.fx * (d[3] - d[1]) + (1.f - sp.fx) * (d[2] - d[0]));
+          const float gx = m * (sp.fy * (d[3] - d[2]) + (1.f - sp.fy) * (d[1] - d[0]));
+          const float gm = cs.w[0] * d[0] + cs.w[1] * d[1] + cs.w[2] * d[2] + cs.w[3] * d[3];
+          a.goff32[ob] = gy;
+          a.goff32[ob + g.HWo] = gx;
+          if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
+            a.gmsk32[(long long)px.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + px.y] =
+                g.msk_logit ? gm * m * (1.f - m) : gm;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) wm[k] = cs.w[k] * m;
+          if (wm[0] == 0.f && wm[1] == 0.f && wm[2] == 0.f && wm[3] == 0.f) rec = -1;
+        }
+        if (a.gq32) {
+          // the lane's record of contributions, corner-major; 16-byte piece p
+          // at position p ^ (lane & 7), so that stores and loads of the rounds
+          // below take the minimum 4 wavefronts
+          float* st = ws->stage[lane];
+          const int sw = lane & 7;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            *reinterpret_cast<float4*>(st + 4 * ((2 * k) ^ sw)) =
+                make_float4(wm[k] * gc[0], wm[k] * gc[1], wm[k] * gc[2], wm[k] * gc[3]);
+            *reinterpret_cast<float4*>(st + 4 * ((2 * k + 1) ^ sw)) =
+                make_float4(wm[k] * gc[4], wm[k] * gc[5], wm[k] * gc[6], wm[k] * gc[7]);
+          }
+          ws->rec[lane] = rec;
+          __syncwarp();
+          // 8 rounds: lanes 8s..8s+7 add the 8 pieces of record (4j + s)
+#pragma unroll 2
+          for (int j = 0; j < 8; ++j) {
+            const int src = 4 * j + (lane >> 3);
+            const int rs = ws->rec[src];
+            if (rs >= 0) {
+              const float4 v = *reinterpret_cast<const float4*>(ws->stage[src] + 4 * (j8 ^ (src & 7)));
+              red_v4(a.gq32 + (uint32_t)rs * 32u + 4 * j8, v.x, v.y, v.z, v.w);
+            }
+          }
+          __syncwarp();  // the staging area is rewritten by the next step
+        }
+      }
+      __syncwarp();  // the next chunk's phase 1 rewrites the slab
     }
   } else if (warp < D_EPI_WARPS && SW == 32) {
     // -------------------------------------------- epilogue, 32-channel slabs
@@ -1052,6 +1221,38 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   }
 }
 
+// ================================================================ corner-quad sum
+// gi32[b][y][x][8o..8o+7] = sum over the four roles of the fp32 corner-quad
+// accumulator: corner 00 of record (y, x), 01 of (y, x-1), 10 of (y-1, x) and
+// 11 of (y-1, x-1).  One thread per (image, pixel, offset group): four
+// 32-byte reads (each record corner read once overall) and one 32-byte write.
+__global__ void quad_sum_kernel(const float* __restrict__ gq, float* __restrict__ gi, int H, int W, int C,
+                                long long n) {
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const int OG = C / 8;
+  const int o = (int)(t % OG);
+  const long long pix = t / OG;  // (b*H + y)*W + x
+  const int x = (int)(pix % W);
+  const long long by = pix / W;
+  const int y = (int)(by % H);
+  const int b = (int)(by / H);
+  // record (y0, x0) -> index ((b*(H+1) + y0+1)*(W+1) + x0+1)*OG + o
+  const long long r00 = (((long long)b * (H + 1) + y + 1) * (W + 1) + x + 1) * OG + o;
+  const long long rows = (long long)(W + 1) * OG;
+  const float4* p0 = reinterpret_cast<const float4*>(gq + r00 * 32);                     // corner 00 of (y, x)
+  const float4* p1 = reinterpret_cast<const float4*>(gq + (r00 - OG) * 32 + 8);          // corner 01 of (y, x-1)
+  const float4* p2 = reinterpret_cast<const float4*>(gq + (r00 - rows) * 32 + 16);       // corner 10 of (y-1, x)
+  const float4* p3 = reinterpret_cast<const float4*>(gq + (r00 - rows - OG) * 32 + 24);  // corner 11 of (y-1, x-1)
+  float4 lo = p0[0], hi = p0[1];
+  const float4 a1 = p1[0], b1 = p1[1], a2 = p2[0], b2 = p2[1], a3 = p3[0], b3 = p3[1];
+  lo.x += a1.x + a2.x + a3.x; lo.y += a1.y + a2.y + a3.y; lo.z += a1.z + a2.z + a3.z; lo.w += a1.w + a2.w + a3.w;
+  hi.x += b1.x + b2.x + b3.x; hi.y += b1.y + b2.y + b3.y; hi.z += b1.z + b2.z + b3.z; hi.w += b1.w + b2.w + b3.w;
+  float4* dst = reinterpret_cast<float4*>(gi + pix * C + o * 8);
+  dst[0] = lo;
+  dst[1] = hi;
+}
+
 // ================================================================ prep / finalize
 // grad_output NCHW [B][Co][HWo] -> gOt [B*HWo][Co]; gb32[co] += tile sums.
 template <typename T>
@@ -1278,19 +1479,32 @@ WgradPlan wgrad_plan(const Geom& g) {
   return w;
 }
 
+// Epilogue slab width of dcn_dgrad_tc_kernel (see the kernel).
+int dgrad_slab_width(const Geom& g) {
+  const bool small_index = (long long)g.B * g.H * g.W * g.C < (1LL << 31);
+  if (g.cpo == 8 && quad_elems(g) < (1LL << 31)) return 8;  // corner-quad records
+  return (g.cpo % 64 == 0 && small_index) ? 64 : (g.cpo % 32 == 0 && small_index) ? 32 : 16;
+}
+
 struct BwdWs {
-  size_t xh, got, wdt, acc, gi32, goff32, gmsk32, gb32, acc_bytes, gwp, total;
+  size_t xh, got, wdt, xq, gi32, acc, gq32, goff32, gmsk32, gb32, acc_bytes, gwp, total;
 };
 BwdWs bwd_ws(const Geom& g, size_t es) {
   BwdWs L;
   const int KB = (g.Cog + 63) / 64;
   const int nkc = (g.Cig / BK) * g.T;
+  const bool quad = dgrad_slab_width(g) == 8;
   size_t o = 0;
   L.xh = o;   o += ws_align(es * (size_t)g.B * g.H * g.W * g.C);
   L.got = o;  o += ws_align(es * (size_t)g.P * g.Co);
   L.wdt = o;  o += ws_align(es * (size_t)g.G * nkc * KB * 4096);
+  // corner-quad epilogue: the input's corner-quad records, and grad_input as
+  // the sum of the accumulator's four roles (written whole: not cleared)
+  L.xq = o;   o += quad ? ws_align(es * (size_t)quad_elems(g)) : 0;
+  L.gi32 = o; o += quad ? ws_align(4 * (size_t)g.B * g.H * g.W * g.C) : 0;
   L.acc = o;  // fp32 accumulators, contiguous so one memset clears them
-  L.gi32 = o;   o += ws_align(4 * (size_t)g.B * g.H * g.W * g.C);
+  L.gq32 = o; o += quad ? ws_align(4 * (size_t)quad_elems(g)) : 0;
+  if (!quad) { L.gi32 = o; o += ws_align(4 * (size_t)g.B * g.H * g.W * g.C); }
   // offset / mask gradient accumulators with the strides of the offset and
   // mask tensors; in the DCNv2 head layout one [B][3*OG*T][HWo] region holds
   // both (no larger than the two separate regions)
@@ -1455,13 +1669,27 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.b_stages = 4;
     // epilogue slab width (see the kernel); the 32-channel variant addresses
     // the input and grad_input with 32-bit element offsets
-    const bool small_index = (long long)g.B * g.H * g.W * g.C < (1LL << 31);
-    const int sw = (g.cpo % 64 == 0 && small_index) ? 64 : (g.cpo % 32 == 0 && small_index) ? 32 : 16;
+    const int sw = dgrad_slab_width(g);
+    a.xq = nullptr;
+    a.gq32 = nullptr;
+    if (sw == 8) {  // corner-quad records of the input for the epilogue's corner reads
+      T* xq = reinterpret_cast<T*>(ws + L.xq);
+      KernelScope ks("quad_records", st);
+      const long long n = quad_elems(g) / 8;
+      quad_records_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xh, xq, g.H, g.W, g.C, n);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      a.xq = xq;
+      a.gq32 = gin ? reinterpret_cast<float*>(ws + L.gq32) : nullptr;
+      a.gi32 = nullptr;
+    }
     while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) --a.b_stages;
     if (dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
     a.idesc = idesc_f16(BM, 64, bf16);
     const int smem = (int)dgrad_smem(KB, a.b_stages, sw).total + 1024;
-    auto kern = sw == 64 ? dcn_dgrad_tc_kernel<T, 64> : sw == 32 ? dcn_dgrad_tc_kernel<T, 32> : dcn_dgrad_tc_kernel<T, 16>;
+    auto kern = sw == 64 ? dcn_dgrad_tc_kernel<T, 64>
+              : sw == 32 ? dcn_dgrad_tc_kernel<T, 32>
+              : sw == 8  ? dcn_dgrad_tc_kernel<T, 8>
+                         : dcn_dgrad_tc_kernel<T, 16>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
       return e;
     // split the K chunks of a tile over ksplit CTAs when that fills the last
@@ -1473,9 +1701,17 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       const double eff = waves / std::ceil(waves);
       if (eff > best + 0.05) { best = eff; ksplit = k; }
     }
-    KernelScope ks("dcn_dgrad_tc", st);
-    kern<<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
+    {
+      KernelScope ks("dcn_dgrad_tc", st);
+      kern<<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (a.gq32) {  // grad_input (channels-last fp32) = the accumulator's four roles
+      KernelScope ks("quad_sum", st);
+      const long long n = (long long)g.B * g.H * g.W * (g.C / 8);
+      quad_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.gq32, gi32, g.H, g.W, g.C, n);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
   }
   // grad_weight and grad_bias are final once the work enqueued so far has run:
   // a caller can start their all-reduce on another stream now.  It then runs

@@ -422,6 +422,31 @@ __host__ __device__ inline long long quad_elems(const Geom& g) {
   return (long long)g.B * (g.H + 1) * (g.W + 1) * g.C * 4;
 }
 
+// channels-last input [B][H][W][C] -> corner-quad records (gather_run_quad):
+// one thread per (record, corner) copies 16 bytes (offset group o's 8
+// channels of one corner, zero outside the image).  Consecutive threads write
+// consecutive 16 bytes and read whole 128-byte pixel rows.
+template <typename T>
+__global__ void quad_records_kernel(const T* __restrict__ xh, T* __restrict__ xq, int H, int W, int C,
+                                    long long n) {
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const int k = (int)(t & 3);
+  const int og8 = C / 8;
+  const long long rec = t >> 2;
+  const int o = (int)(rec % og8);
+  const long long pix = rec / og8;  // ((b*(H+1) + y0+1)*(W+1) + x0+1)
+  const int xx = (int)(pix % (W + 1));
+  const long long by = pix / (W + 1);
+  const int yy = (int)(by % (H + 1));
+  const int b = (int)(by / (H + 1));
+  const int y = yy - 1 + (k >> 1), x = xx - 1 + (k & 1);
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (y >= 0 && y < H && x >= 0 && x < W)
+    v = *reinterpret_cast<const uint4*>(xh + (((long long)b * H + y) * W + x) * C + o * 8);
+  reinterpret_cast<uint4*>(xq)[t] = v;
+}
+
 // Producer for offset groups of exactly 8 channels (one group per lane's
 // 16-byte channel vector): lanes and rows as gather_run, each sample read from
 // its corner-quad record with two 256-bit loads.  Same stage protocol and
