@@ -162,7 +162,9 @@ static SimtBwdLayout simt_bwd_layout(const dcn_conv_desc* d, const Geom& g) {
   const bool f32 = d->dtype == DCN_FLOAT32;
   size_t off = 0;
   L.gcol = off;  off += ws_align(sizeof(float) * (size_t)g.C * g.T * (size_t)g.P);
-  L.gin32 = off; off += f32 ? 0 : ws_align(sizeof(float) * (size_t)g.B * g.C * g.H * g.W);
+  // fp32 grad_input accumulator: NCHW for fp16/bf16 on the scalar scatter,
+  // channels-last for the four-channel scatter (every dtype)
+  L.gin32 = off; off += ws_align(sizeof(float) * (size_t)g.B * g.C * g.H * g.W);
   L.gw32 = off;  off += f32 ? 0 : ws_align(sizeof(float) * (size_t)g.Co * g.Cig * g.T);
   L.goff = off;  off += ws_align(elem_size(d->dtype) * (size_t)g.B * g.OG * 2 * g.T * g.HWo);
   L.total = off;
@@ -457,6 +459,7 @@ static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const 
   SimtBackwardWs ws;
   ws.gcol = (float*)(base + L.gcol);
   ws.gin32 = f32 ? nullptr : (float*)(base + L.gin32);
+  ws.gacc = (float*)(base + L.gin32);
   ws.gw32 = f32 ? nullptr : (float*)(base + L.gw32);
   ws.goff_scratch = base + L.goff;
   cudaError_t e = cudaSuccess;

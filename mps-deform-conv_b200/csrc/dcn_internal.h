@@ -9,6 +9,7 @@ namespace dcn {
 struct SimtBackwardWs {
   float* gcol;          // [C*T][P] column gradient
   float* gin32;         // [B][C][H][W] fp32 grad_input accumulator (NULL when T is float)
+  float* gacc;          // [B][H][W][C] fp32 channels-last grad_input accumulator, or NULL
   float* gw32;          // [Co][C/G*T] fp32 grad_weight accumulator (NULL when T is float)
   void* goff_scratch;   // offset-grad sink when the caller wants only grad_mask
 };

@@ -220,6 +220,60 @@ __global__ void col2im_kernel(Geom g, const TC* __restrict__ gcol, const T* __re
   }
 }
 
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// grad_input (channels-last fp32 [B][H][W][C], zeroed) += col2im(gcol), four
+// channels of one sample per thread: the sampling point once for the four,
+// and one 16-byte red.global.add.v4.f32 per corner (a quarter of
+// col2im_kernel's reduction requests).  C and the channels per offset group
+// are multiples of 4; acc is 16-byte aligned.
+template <typename TC, typename T>
+__global__ void col2im_nhwc4_kernel(Geom g, const TC* __restrict__ gcol, const T* __restrict__ off,
+                                    const T* __restrict__ msk, float* __restrict__ acc) {
+  const long long total = (long long)(g.C / 4) * g.T * g.P;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long row = e / g.P, n = e - row * g.P;  // row = (c/4)*T + t
+    const int c4 = (int)(row / g.T), t = (int)(row - (long long)c4 * g.T);
+    const int c = 4 * c4;
+    const int b = (int)(n / g.HWo), p = (int)(n - (long long)b * g.HWo);
+    float m;
+    const SamplePos sp = sample_point(g, off, msk, b, c / g.cpo, t, p, &m);
+    const Corners cs = corners_of(sp, g.H, g.W);
+    const long long rs = (long long)g.T * g.P;  // channel c -> c + 1 in the column layout
+    const TC* src = gcol + ((long long)c * g.T + t) * g.P + n;
+    const float v0 = m * to_f(src[0]), v1 = m * to_f(src[rs]), v2 = m * to_f(src[2 * rs]), v3 = m * to_f(src[3 * rs]);
+    float* base = acc + (long long)b * g.H * g.W * g.C + c;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float w = cs.w[k];
+      if (w != 0.0f) red_add_v4(base + (long long)cs.idx[k] * g.C, w * v0, w * v1, w * v2, w * v3);
+    }
+  }
+}
+
+// channels-last fp32 [B][HW][C] -> NCHW T [B][C][HW], 32 x 32 tiles through
+// shared memory (33-word rows).  grid (HW/32, C/32, B), 256 threads.
+template <typename T>
+__global__ void nhwc_f32_to_nchw_kernel(const float* __restrict__ src, T* __restrict__ dst, int C, int HW) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z, c0 = blockIdx.y * 32, hw0 = blockIdx.x * 32;
+  const float* s = src + (long long)b * HW * C;
+  T* d = dst + (long long)b * C * HW;
+  for (int e = threadIdx.x; e < 32 * 32; e += blockDim.x) {
+    const int hh = e >> 5, cc = e & 31;
+    if (hw0 + hh < HW && c0 + cc < C) tile[cc][hh] = s[(long long)(hw0 + hh) * C + c0 + cc];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 32 * 32; e += blockDim.x) {
+    const int cc = e >> 5, hh = e & 31;
+    if (hw0 + hh < HW && c0 + cc < C) d[(long long)(c0 + cc) * HW + hw0 + hh] = from_f<T>(tile[cc][hh]);
+  }
+}
+
 // grad_offset / grad_mask, one thread per (b, offset group, tap, pixel).
 template <typename TC, typename T>
 __global__ void col2im_coord_kernel(Geom g, const TC* __restrict__ gcol, const T* __restrict__ x,
@@ -456,11 +510,26 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
     if ((e = launch_simt_gemm<false, false>("simt_dgrad_gemm", la, lb, ep, Kg, (int)g.P, g.Cog, g.G, 1, st)) != cudaSuccess)
       return e;
     if (gin) {
-      float* gin32 = ws.gin32 ? ws.gin32 : reinterpret_cast<float*>(gin);
       const long long n = (long long)g.B * g.C * g.H * g.W;
-      if ((e = cudaMemsetAsync(gin32, 0, sizeof(float) * (size_t)n, st)) != cudaSuccess) return e;
-      if ((e = simt_col2im<float, T>(g, ws.gcol, off, msk, gin32, st)) != cudaSuccess) return e;
-      if (ws.gin32 && (e = convert_f32<T>(ws.gin32, gin, n, st)) != cudaSuccess) return e;
+      if (ws.gacc && g.C % 4 == 0 && g.cpo % 4 == 0 && n > 0) {
+        // four channels per thread into a channels-last accumulator, then NCHW
+        if ((e = cudaMemsetAsync(ws.gacc, 0, sizeof(float) * (size_t)n, st)) != cudaSuccess) return e;
+        {
+          KernelScope ks("col2im_nhwc4", st);
+          col2im_nhwc4_kernel<float, T><<<grid_for((long long)(g.C / 4) * g.T * g.P), 256, 0, st>>>(
+              g, ws.gcol, off, msk, ws.gacc);
+        }
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        KernelScope ks("nhwc_f32_to_nchw", st);
+        const dim3 grid((unsigned)((g.H * g.W + 31) / 32), (unsigned)((g.C + 31) / 32), (unsigned)g.B);
+        nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(ws.gacc, gin, g.C, g.H * g.W);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      } else {
+        float* gin32 = ws.gin32 ? ws.gin32 : reinterpret_cast<float*>(gin);
+        if ((e = cudaMemsetAsync(gin32, 0, sizeof(float) * (size_t)n, st)) != cudaSuccess) return e;
+        if ((e = simt_col2im<float, T>(g, ws.gcol, off, msk, gin32, st)) != cudaSuccess) return e;
+        if (ws.gin32 && (e = convert_f32<T>(ws.gin32, gin, n, st)) != cudaSuccess) return e;
+      }
     }
     if (goff || gmsk) {
       T* goff_t = goff ? goff : reinterpret_cast<T*>(ws.goff_scratch);

@@ -358,7 +358,7 @@ bool tc_forward_supported(const dcn_conv_desc& d, const Geom& g) {
 
 // Offset groups of 8 channels gather from corner-quad records (32-bit
 // element offsets).
-static bool use_quad(const Geom& g) { return g.cpo == 8 && quad_elems(g) < (1LL << 31); }
+static bool use_quad(const Geom& g) { return quad_ok(g); }
 
 struct FwdWs {
   size_t xh, wsw, xq, total;
@@ -382,7 +382,8 @@ SavedLayout saved_layout(const Geom& g) {
   const size_t nkc = (size_t)(g.Cig / BK) * g.T;
   L.xh = 0;
   L.cols = ws_align(2 * (size_t)g.B * g.H * g.W * g.C);
-  L.total = L.cols + ws_align((size_t)g.G * n_tiles * nkc * A_STAGE_BYTES);
+  L.xq = L.cols + ws_align((size_t)g.G * n_tiles * nkc * A_STAGE_BYTES);
+  L.total = L.xq + (use_quad(g) ? ws_align(2 * (size_t)quad_elems(g)) : 0);
   return L;
 }
 
@@ -487,11 +488,11 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   const bool quad = use_quad(g) && (reinterpret_cast<uintptr_t>(xh) & 15) == 0;
-  T* xq = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.xq);
+  // training: the records stay with the saved state for the backward's corner reads
+  T* xq = reinterpret_cast<T*>(saved ? static_cast<char*>(saved) + SV.xq : static_cast<char*>(workspace) + L.xq);
   if (quad) {
     KernelScope ks("quad_records", st);
-    const long long n = quad_elems(g) / 8;  // 16-byte pieces
-    quad_records_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xh, xq, g.H, g.W, g.C, n);
+    quad_records_launch(xh, xq, g, st);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
 

@@ -19,8 +19,9 @@ size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g);
 //         each tile [128 pixels][64 channels] in the 128-byte-swizzled
 //         shared-memory image, so the weight-gradient GEMM streams them back
 //         with bulk copies instead of gathering again.
+//   xq    corner-quad records of the input (offset groups of 8 channels)
 struct SavedLayout {
-  size_t xh, cols, total;
+  size_t xh, cols, xq, total;
 };
 SavedLayout saved_layout(const Geom& g);
 

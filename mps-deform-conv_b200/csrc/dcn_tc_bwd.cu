@@ -765,11 +765,26 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         if (lane == 0) mbar_arrive(d_empty(e));  // TMEM buffer read completely
       }
       __syncwarp();
-      // ---- phase 2: lane = (pixel, offset group), 4 pixels per step
+      // ---- phase 2: lane = (pixel, offset group), 4 pixels per step; the
+      // offsets and mask of step it+1 are loaded during step it
+      auto load_sample = [&](int row, T& dy, T& dx, T& mr) {
+        const int4 p4 = ws->pix[row];
+        if (p4.x >= 0) {
+          const long long ob = (long long)p4.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + p4.y;
+          dy = off[ob];
+          dx = off[ob + g.HWo];
+          mr = g.use_mask ? msk[(long long)p4.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + p4.y]
+                          : from_f<T>(1.f);
+        }
+      };
+      T ndy = from_f<T>(0.f), ndx = from_f<T>(0.f), nmr = from_f<T>(1.f);
+      load_sample(rsub, ndy, ndx, nmr);
 #pragma unroll 1
       for (int it = 0; it < 8; ++it) {
         const int rr = it * 4 + rsub;
         const int4 px = ws->pix[rr];
+        const T cdy = ndy, cdx = ndx, cmr = nmr;
+        if (it + 1 < 8) load_sample(rr + 4, ndy, ndx, nmr);
         const uint4 gd = *reinterpret_cast<const uint4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2));
         float gc[8];
         {
@@ -782,10 +797,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         float wm[4] = {0.f, 0.f, 0.f, 0.f};
         if (px.x >= 0) {
           const long long ob = (long long)px.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + px.y;
-          const float dy = to_f(off[ob]), dx = to_f(off[ob + g.HWo]);
-          const float m = g.use_mask ? mask_of(g, to_f(msk[(long long)px.x * g.msk_bs +
-                                                           (long long)(o * g.T + kw.t) * g.HWo + px.y]))
-                                     : 1.f;
+          const float dy = to_f(cdy), dx = to_f(cdx);
+          const float m = g.use_mask ? mask_of(g, to_f(cmr)) : 1.f;
           const SamplePos sp = sample_pos(px.z + kw.ti * g.dh, px.w + kw.tj * g.dw, dy, dx);
           const Corners cs = corners_of(sp, g.H, g.W);
           // the record covers every corner of a sample whose floor lies in
@@ -1482,7 +1495,7 @@ WgradPlan wgrad_plan(const Geom& g) {
 // Epilogue slab width of dcn_dgrad_tc_kernel (see the kernel).
 int dgrad_slab_width(const Geom& g) {
   const bool small_index = (long long)g.B * g.H * g.W * g.C < (1LL << 31);
-  if (g.cpo == 8 && quad_elems(g) < (1LL << 31)) return 8;  // corner-quad records
+  if (quad_ok(g)) return 8;  // corner-quad records (the forward keeps them in the training state)
   return (g.cpo % 64 == 0 && small_index) ? 64 : (g.cpo % 32 == 0 && small_index) ? 32 : 16;
 }
 
@@ -1500,7 +1513,7 @@ BwdWs bwd_ws(const Geom& g, size_t es) {
   L.wdt = o;  o += ws_align(es * (size_t)g.G * nkc * KB * 4096);
   // corner-quad epilogue: the input's corner-quad records, and grad_input as
   // the sum of the accumulator's four roles (written whole: not cleared)
-  L.xq = o;   o += quad ? ws_align(es * (size_t)quad_elems(g)) : 0;
+  L.xq = o;   o += quad ? ws_align(es * (size_t)quad_elems(g)) : 0;  // when not kept by the forward
   L.gi32 = o; o += quad ? ws_align(4 * (size_t)g.B * g.H * g.W * g.C) : 0;
   L.acc = o;  // fp32 accumulators, contiguous so one memset clears them
   L.gq32 = o; o += quad ? ws_align(4 * (size_t)quad_elems(g)) : 0;
@@ -1673,11 +1686,15 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     a.xq = nullptr;
     a.gq32 = nullptr;
     if (sw == 8) {  // corner-quad records of the input for the epilogue's corner reads
-      T* xq = reinterpret_cast<T*>(ws + L.xq);
-      KernelScope ks("quad_records", st);
-      const long long n = quad_elems(g) / 8;
-      quad_records_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xh, xq, g.H, g.W, g.C, n);
-      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      T* xq;
+      if (saved) {  // the forward's, kept with the training state
+        xq = reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.xq);
+      } else {
+        xq = reinterpret_cast<T*>(ws + L.xq);
+        KernelScope ks("quad_records", st);
+        quad_records_launch(xh, xq, g, st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      }
       a.xq = xq;
       a.gq32 = gin ? reinterpret_cast<float*>(ws + L.gq32) : nullptr;
       a.gi32 = nullptr;

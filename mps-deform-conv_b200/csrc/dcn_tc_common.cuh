@@ -421,30 +421,39 @@ __device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restri
 __host__ __device__ inline long long quad_elems(const Geom& g) {
   return (long long)g.B * (g.H + 1) * (g.W + 1) * g.C * 4;
 }
+// The forward and the backward take the corner-quad path together: offset
+// groups of 8 channels, 32-bit record offsets, one record row per grid row.
+__host__ __device__ inline bool quad_ok(const Geom& g) {
+  return g.cpo == 8 && quad_elems(g) < (1LL << 31) && (long long)g.B * (g.H + 1) <= 65535;
+}
 
 // channels-last input [B][H][W][C] -> corner-quad records (gather_run_quad):
-// one thread per (record, corner) copies 16 bytes (offset group o's 8
-// channels of one corner, zero outside the image).  Consecutive threads write
-// consecutive 16 bytes and read whole 128-byte pixel rows.
+// blockIdx.y = b*(H+1) + y0+1 is one row of records; its threads copy
+// 16 bytes each (offset group o's 8 channels of one corner, zero outside the
+// image), consecutive threads writing consecutive 16 bytes and reading whole
+// 128-byte pixel rows.
 template <typename T>
-__global__ void quad_records_kernel(const T* __restrict__ xh, T* __restrict__ xq, int H, int W, int C,
-                                    long long n) {
-  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  if (t >= n) return;
-  const int k = (int)(t & 3);
-  const int og8 = C / 8;
-  const long long rec = t >> 2;
-  const int o = (int)(rec % og8);
-  const long long pix = rec / og8;  // ((b*(H+1) + y0+1)*(W+1) + x0+1)
-  const int xx = (int)(pix % (W + 1));
-  const long long by = pix / (W + 1);
-  const int yy = (int)(by % (H + 1));
-  const int b = (int)(by / (H + 1));
-  const int y = yy - 1 + (k >> 1), x = xx - 1 + (k & 1);
-  uint4 v = make_uint4(0, 0, 0, 0);
-  if (y >= 0 && y < H && x >= 0 && x < W)
-    v = *reinterpret_cast<const uint4*>(xh + (((long long)b * H + y) * W + x) * C + o * 8);
-  reinterpret_cast<uint4*>(xq)[t] = v;
+__global__ void quad_records_kernel(const T* __restrict__ xh, T* __restrict__ xq, int H, int W, int C) {
+  const int yy = blockIdx.y % (H + 1), b = blockIdx.y / (H + 1);
+  const int per_pix = C / 2;  // 16-byte pieces per record position: (C/8 groups) x 4 corners
+  const int n = (W + 1) * per_pix;
+  uint4* dst = reinterpret_cast<uint4*>(xq) + (size_t)blockIdx.y * n;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    const int xx = e / per_pix, r = e - xx * per_pix;
+    const int o = r >> 2, k = r & 3;
+    const int y = yy - 1 + (k >> 1), x = xx - 1 + (k & 1);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (y >= 0 && y < H && x >= 0 && x < W)
+      v = *reinterpret_cast<const uint4*>(xh + (((size_t)b * H + y) * W + x) * C + o * 8);
+    dst[e] = v;
+  }
+}
+
+template <typename T>
+inline void quad_records_launch(const T* xh, T* xq, const Geom& g, cudaStream_t st) {
+  const int n = (g.W + 1) * (g.C / 2);
+  const dim3 grid((unsigned)((n + 255) / 256), (unsigned)(g.B * (g.H + 1)));
+  quad_records_kernel<T><<<grid, 256, 0, st>>>(xh, xq, g.H, g.W, g.C);
 }
 
 // Producer for offset groups of exactly 8 channels (one group per lane's
