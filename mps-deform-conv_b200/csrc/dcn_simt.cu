@@ -93,14 +93,118 @@ simt_gemm_kernel(LA la, LB lb, EP ep, int M, int N, int K, int splits, int k_per
     }
 }
 
+// The same GEMM with 128 x 128 x 8 tiles, 8 x 8 accumulators per thread
+// (four times the FMAs per shared-memory load of the 64 x 64 kernel) and the
+// next K tile's global loads in registers while the current tile computes
+// (double-buffered shared memory, one barrier per K tile).  Thread (tx, ty)
+// owns rows {4ty..4ty+3, 64+4ty..64+4ty+3} and the same pattern of columns,
+// so its operand reads are two float4 per matrix per k, broadcast or on
+// distinct banks.
+constexpr int BG_BM = 128, BG_BN = 128, BG_BK = 8, BG_THREADS = 256;
+
+template <bool KFAST, int BMN, class L>
+__device__ __forceinline__ void bg_load_regs(float (&r)[4], const L& ld, int g, int k0, int kend, int mn0,
+                                             int mnend, int tid) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = tid + i * BG_THREADS;
+    int kk, mn;
+    if (KFAST) { kk = e % BG_BK; mn = e / BG_BK; }
+    else       { mn = e % BMN; kk = e / BMN; }
+    const int k = k0 + kk, j = mn0 + mn;
+    r[i] = (k < kend && j < mnend) ? ld(g, k, j) : 0.0f;
+  }
+}
+template <bool KFAST, int BMN>
+__device__ __forceinline__ void bg_store_regs(float (*S)[BMN + 4], const float (&r)[4], int tid) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = tid + i * BG_THREADS;
+    int kk, mn;
+    if (KFAST) { kk = e % BG_BK; mn = e / BG_BK; }
+    else       { mn = e % BMN; kk = e / BMN; }
+    S[kk][mn] = r[i];
+  }
+}
+
+template <bool A_KFAST, bool B_KFAST, class LA, class LB, class EP>
+__global__ void __launch_bounds__(BG_THREADS)
+simt_gemm_big_kernel(LA la, LB lb, EP ep, int M, int N, int K, int splits, int k_per_split) {
+  __shared__ __align__(16) float As[2][BG_BK][BG_BM + 4];
+  __shared__ __align__(16) float Bs[2][BG_BK][BG_BN + 4];
+  const int tid = threadIdx.x;
+  const int g = blockIdx.z / splits, s = blockIdx.z % splits;
+  const int m0 = blockIdx.y * BG_BM, n0 = blockIdx.x * BG_BN;
+  const int kbeg = s * k_per_split;
+  const int kend = min(K, kbeg + k_per_split);
+  const int tx = tid % 16, ty = tid / 16;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  float ra[4], rb[4];
+  if (kbeg < kend) {
+    bg_load_regs<A_KFAST, BG_BM>(ra, la, g, kbeg, kend, m0, M, tid);
+    bg_load_regs<B_KFAST, BG_BN>(rb, lb, g, kbeg, kend, n0, N, tid);
+    bg_store_regs<A_KFAST, BG_BM>(As[0], ra, tid);
+    bg_store_regs<B_KFAST, BG_BN>(Bs[0], rb, tid);
+  }
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = kbeg; k0 < kend; k0 += BG_BK) {
+    const bool more = k0 + BG_BK < kend;
+    if (more) {  // the next tile's loads are in flight during this tile's FMAs
+      bg_load_regs<A_KFAST, BG_BM>(ra, la, g, k0 + BG_BK, kend, m0, M, tid);
+      bg_load_regs<B_KFAST, BG_BN>(rb, lb, g, k0 + BG_BK, kend, n0, N, tid);
+    }
+#pragma unroll
+    for (int kk = 0; kk < BG_BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (more) {
+      bg_store_regs<A_KFAST, BG_BM>(As[buf ^ 1], ra, tid);
+      bg_store_regs<B_KFAST, BG_BN>(Bs[buf ^ 1], rb, tid);
+    }
+    __syncthreads();
+    buf ^= 1;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+      const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (m < M && n < N) ep(g, m, n, acc[i][j]);
+    }
+}
+
+// 128 x 128 tiles when they alone give at least a wave of CTAs (148 SMs),
+// else 64 x 64 tiles.
 template <bool A_KFAST, bool B_KFAST, class LA, class LB, class EP>
 static cudaError_t launch_simt_gemm(const char* name, const LA& la, const LB& lb, const EP& ep,
                                     int M, int N, int K, int groups, int splits, cudaStream_t st) {
   if (M <= 0 || N <= 0 || groups <= 0) return cudaSuccess;
-  const int kps = ((K + splits - 1) / splits + SG_BK - 1) / SG_BK * SG_BK;
-  dim3 grid((N + SG_BN - 1) / SG_BN, (M + SG_BM - 1) / SG_BM, groups * splits);
+  const long long big_ctas = (long long)((N + BG_BN - 1) / BG_BN) * ((M + BG_BM - 1) / BG_BM) * groups * splits;
   KernelScope ks(name, st);
-  simt_gemm_kernel<A_KFAST, B_KFAST><<<grid, SG_THREADS, 0, st>>>(la, lb, ep, M, N, K, splits, kps);
+  if (big_ctas >= 148) {
+    const int kps = ((K + splits - 1) / splits + BG_BK - 1) / BG_BK * BG_BK;
+    dim3 grid((N + BG_BN - 1) / BG_BN, (M + BG_BM - 1) / BG_BM, groups * splits);
+    simt_gemm_big_kernel<A_KFAST, B_KFAST><<<grid, BG_THREADS, 0, st>>>(la, lb, ep, M, N, K, splits, kps);
+  } else {
+    const int kps = ((K + splits - 1) / splits + SG_BK - 1) / SG_BK * SG_BK;
+    dim3 grid((N + SG_BN - 1) / SG_BN, (M + SG_BM - 1) / SG_BM, groups * splits);
+    simt_gemm_kernel<A_KFAST, B_KFAST><<<grid, SG_THREADS, 0, st>>>(la, lb, ep, M, N, K, splits, kps);
+  }
   return cudaGetLastError();
 }
 
@@ -128,19 +232,29 @@ struct ColumnLoader {  // B(k, n) = col[(g*Cig + k/T)*T + k%T][n]   (forward)
     return column_value(geo, x, off, msk, b, g * geo.Cig + cl, t, p);
   }
 };
+// n / d for 0 <= n: a float-reciprocal quotient corrected to the exact one
+// (n < 2^24), else the integer division.
+__device__ __forceinline__ int div_rcp(int n, int d, float rcp) {
+  if (n >= (1 << 24)) return n / d;
+  int q = __float2int_rz((float)n * rcp);
+  const int r = n - q * d;
+  if (r < 0) --q;
+  else if (r >= d) ++q;
+  return q;
+}
 template <typename T>
 struct GradOutLoaderCN {  // B(co, n=px) = gO[b][g*Cog + co][p]   (dgrad)
-  Geom geo; const T* go;
+  Geom geo; const T* go; float rcp_hwo;
   __device__ float operator()(int g, int co, int n) const {
-    const int b = n / geo.HWo, p = n - b * geo.HWo;
+    const int b = div_rcp(n, geo.HWo, rcp_hwo), p = n - b * geo.HWo;
     return to_f(go[((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p]);
   }
 };
 template <typename T>
 struct GradOutLoaderPM {  // A(px, m=co) = gO[b][g*Cog + co][p]   (wgrad)
-  Geom geo; const T* go;
+  Geom geo; const T* go; float rcp_hwo;
   __device__ float operator()(int g, int px, int co) const {
-    const int b = px / geo.HWo, p = px - b * geo.HWo;
+    const int b = div_rcp(px, geo.HWo, rcp_hwo), p = px - b * geo.HWo;
     return to_f(go[((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p]);
   }
 };
@@ -374,10 +488,19 @@ __global__ void simt_fwd_reduce_kernel(Geom g, const float* __restrict__ part, i
 
 static int simt_fwd_splits(const Geom& g) {
   const long long tiles = ((g.P + SG_BN - 1) / SG_BN) * ((g.Cog + SG_BM - 1) / SG_BM) * g.G;
-  if (tiles == 0 || tiles >= 148) return 1;  // empty batch, or at least one wave
+  if (tiles == 0) return 1;  // empty batch
+  // the 128 x 128 tiles of launch_simt_gemm: split K until they make a wave
+  const long long big = ((g.P + BG_BN - 1) / BG_BN) * ((g.Cog + BG_BM - 1) / BG_BM) * g.G;
+  if (big >= 148) return 1;
+  const int big_ksteps = (g.Cig * g.T + BG_BK - 1) / BG_BK;
+  int splits = (int)((148 + big - 1) / big);
+  if (splits > big_ksteps / 8) splits = big_ksteps / 8;  // at least 8 K steps per split
+  if (splits >= 2 && big * splits >= 148) return splits;
+  // else the 64 x 64 tiles: a wave of them, at least 4 K steps per split
+  if (tiles >= 148) return 1;
   const int ksteps = (g.Cig * g.T + SG_BK - 1) / SG_BK;
-  int splits = (int)((148 + tiles - 1) / tiles);
-  if (splits > ksteps / 4) splits = ksteps / 4;  // at least 4 K steps per split
+  splits = (int)((148 + tiles - 1) / tiles);
+  if (splits > ksteps / 4) splits = ksteps / 4;
   return splits < 2 ? 1 : splits;
 }
 
@@ -489,7 +612,7 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
     const long long max_splits = (g.P + 255) / 256;
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
-    GradOutLoaderPM<T> la{g, go};
+    GradOutLoaderPM<T> la{g, go, 1.f / (float)g.HWo};
     AtomicWeightEpilogue ep{gw32, g.Cog, Kg};
     // the columns, one sample per (pixel, tap, offset group), in the column
     // gradient's buffer (free until the dgrad GEMM below writes it)
@@ -505,7 +628,7 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
   }
   if (gin || goff || gmsk) {
     WeightColLoader<T> la{w, g.Cog, Kg};
-    GradOutLoaderCN<T> lb{g, go};
+    GradOutLoaderCN<T> lb{g, go, 1.f / (float)g.HWo};
     ColumnStoreEpilogue ep{ws.gcol, Kg, g.P};
     if ((e = launch_simt_gemm<false, false>("simt_dgrad_gemm", la, lb, ep, Kg, (int)g.P, g.Cog, g.G, 1, st)) != cudaSuccess)
       return e;

@@ -412,6 +412,8 @@ struct DgradArgs {
   float* goff32;     // [B][OG*2T][HWo], zeroed
   float* gmsk32;     // [B][OG*T][HWo], zeroed (null without mask)
   const void* xq;    // quad epilogue (SW = 8): corner-quad records of the input
+  void* goff_t;      // quad epilogue: grad_offset / grad_mask in the caller's dtype, written
+  void* gmsk_t;      //   directly (each value has one writer); null when not wanted
   float* gq32;       // quad epilogue: fp32 corner-quad accumulator, zeroed (null: no grad_input)
   int* status;
   Geom g;
@@ -824,11 +826,14 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           const float gy = m * (sp.fx * (d[3] - d[1]) + (1.f - sp.fx) * (d[2] - d[0]));
           const float gx = m * (sp.fy * (d[3] - d[2]) + (1.f - sp.fy) * (d[1] - d[0]));
           const float gm = cs.w[0] * d[0] + cs.w[1] * d[1] + cs.w[2] * d[2] + cs.w[3] * d[3];
-          a.goff32[ob] = gy;
-          a.goff32[ob + g.HWo] = gx;
-          if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
-            a.gmsk32[(long long)px.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + px.y] =
-                g.msk_logit ? gm * m * (1.f - m) : gm;
+          if (a.goff_t) {
+            T* go_ = static_cast<T*>(a.goff_t);
+            go_[ob] = from_f<T>(gy);
+            go_[ob + g.HWo] = from_f<T>(gx);
+          }
+          if (a.gmsk_t)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
+            static_cast<T*>(a.gmsk_t)[(long long)px.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + px.y] =
+                from_f<T>(g.msk_logit ? gm * m * (1.f - m) : gm);
 #pragma unroll
           for (int k = 0; k < 4; ++k) wm[k] = cs.w[k] * m;
           if (wm[0] == 0.f && wm[1] == 0.f && wm[2] == 0.f && wm[3] == 0.f) rec = -1;
@@ -1521,8 +1526,9 @@ BwdWs bwd_ws(const Geom& g, size_t es) {
   // offset / mask gradient accumulators with the strides of the offset and
   // mask tensors; in the DCNv2 head layout one [B][3*OG*T][HWo] region holds
   // both (no larger than the two separate regions)
-  L.goff32 = o; o += ws_align(4 * (size_t)g.B * g.off_bs);
-  L.gmsk32 = o; o += g.msk_logit ? 0 : ws_align(4 * (size_t)g.B * g.msk_bs);
+  // (the quad epilogue writes the offset and mask gradients directly)
+  L.goff32 = o; o += quad ? 0 : ws_align(4 * (size_t)g.B * g.off_bs);
+  L.gmsk32 = o; o += (quad || g.msk_logit) ? 0 : ws_align(4 * (size_t)g.B * g.msk_bs);
   L.gb32 = o;   o += ws_align(4 * (size_t)g.Co);
   L.acc_bytes = o - L.acc;
   L.gwp = o;  // written whole by the wgrad kernels: not cleared
@@ -1678,6 +1684,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     DgradArgs a;
     a.xh = xh; a.off = off; a.msk = g.use_mask ? msk : nullptr; a.wdt = wdt;
     a.gi32 = gi32; a.goff32 = goff32; a.gmsk32 = g.use_mask ? gmsk32 : nullptr;
+    a.goff_t = a.gmsk_t = nullptr;
     a.status = status; a.g = g; a.nkc = nkc; a.kb = KB;
     a.b_stages = 4;
     // epilogue slab width (see the kernel); the 32-channel variant addresses
@@ -1698,6 +1705,9 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       a.xq = xq;
       a.gq32 = gin ? reinterpret_cast<float*>(ws + L.gq32) : nullptr;
       a.gi32 = nullptr;
+      a.goff_t = goff;
+      a.gmsk_t = g.use_mask ? gmsk : nullptr;
+      a.goff32 = a.gmsk32 = nullptr;
     }
     while (a.b_stages > 2 && dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) --a.b_stages;
     if (dgrad_smem(KB, a.b_stages, sw).total + 1024 > 225 * 1024) return cudaErrorInvalidConfiguration;
@@ -1748,12 +1758,15 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {  // offset / mask (and channels-last input) gradients: fp32 -> T in one launch
+     // (the quad epilogue wrote the offset and mask gradients already)
+    const bool off_done = need_d && dgrad_slab_width(g) == 8;
     ConvertJobs jobs{};
     auto add = [&](const float* src, void* dst, long long n) {
       if (dst && n > 0) { jobs.src[jobs.n] = src; jobs.dst[jobs.n] = dst; jobs.count[jobs.n] = n; ++jobs.n; }
     };
     if (gin && g.in_nhwc) add(gi32, gin, (long long)g.B * g.H * g.W * g.C);  // channels-last: no transpose
-    if (g.msk_logit) {  // DCNv2 head layout: goff is the whole [B][3*OG*T][HWo] gradient
+    if (off_done) {
+    } else if (g.msk_logit) {  // DCNv2 head layout: goff is the whole [B][3*OG*T][HWo] gradient
       add(goff32, goff, (long long)g.B * g.off_bs);
     } else {
       add(goff32, goff, (long long)g.B * g.OG * 2 * g.T * g.HWo);

@@ -91,8 +91,10 @@ def test_workspace_sizes_are_host_queries():
     # group) threads the forward also materializes fp32 columns [C*T][P]
     small = _desc(input_shape=(1, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1))
     assert lib.dcn_forward_workspace_size(ctypes.byref(small)) == 9 * 64 * 256 * 4
+    # 2x128x64x64: fp32 columns [C*T][P], and K split 3 ways so that its 64
+    # tiles of 128 x 128 make a wave (3 fp32 partial outputs [Co][P])
     c2 = _desc(input_shape=(2, 128, 64, 64), weight_shape=(128, 128, 3, 3), padding=(1, 1), use_mask=True)
-    assert lib.dcn_forward_workspace_size(ctypes.byref(c2)) == 128 * 9 * 8192 * 4
+    assert lib.dcn_forward_workspace_size(ctypes.byref(c2)) == 128 * 9 * 8192 * 4 + 3 * 128 * 8192 * 4
 
 
 def test_forward_rejects_null_and_small_workspace_without_launching():

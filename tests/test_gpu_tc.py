@@ -135,15 +135,20 @@ def test_tc_layout_passes_unaligned_pointers(dtype, cuda):
     assert_close(u, ref, dtype, 'u')
 
 
-@pytest.mark.parametrize("mask_sel", [(1, 0, 0, 0, 0), (0, 1, 0, 0, 1), (0, 0, 1, 1, 0)])
-def test_tc_backward_output_subsets(mask_sel, cuda):
-    """Only the requested gradients are computed and they match the full call."""
+@pytest.mark.parametrize("name", ["c128_g2_og4_dil2", "c64_og8_near_int"])
+@pytest.mark.parametrize("mask_sel", [(1, 0, 0, 0, 0), (0, 1, 0, 0, 1), (0, 0, 1, 1, 0), (0, 0, 1, 0, 0),
+                                      (0, 0, 0, 1, 0)])
+def test_tc_backward_output_subsets(mask_sel, name, cuda):
+    """Only the requested gradients are computed and they match the full call
+    (c64_og8_near_int takes the corner-quad epilogue, which writes the offset and
+    mask gradients directly; c128_g2_og4_dil2 the 32-channel one)."""
     import mps_deform_conv as mdc
     lib = mdc._get_lib()
-    T = _make(SHAPES["c128_g2_og4_dil2"], torch.bfloat16, cuda, seed=5)
+    spec = SHAPES[name]
+    T = _make(spec, torch.bfloat16, cuda, seed=5)
     st, pd, dl = T["stride"], T["padding"], T["dilation"]
     args = (T["grad_output"], T["input"], T["weight"], T["offset"], T["mask"], T["bias"],
-            st[0], st[1], pd[0], pd[1], dl[0], dl[1], 2, 4, True)
+            st[0], st[1], pd[0], pd[1], dl[0], dl[1], spec[5], spec[6], True)
     full = lib.deform_conv2d_backward(*args, [True] * 5)
     part = lib.deform_conv2d_backward(*args, [bool(v) for v in mask_sel])
     torch.cuda.synchronize()
