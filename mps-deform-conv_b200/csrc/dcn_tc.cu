@@ -383,7 +383,8 @@ SavedLayout saved_layout(const Geom& g) {
   L.xh = 0;
   L.cols = ws_align(2 * (size_t)g.B * g.H * g.W * g.C);
   L.xq = L.cols + ws_align((size_t)g.G * n_tiles * nkc * A_STAGE_BYTES);
-  L.total = L.xq + (use_quad(g) ? ws_align(2 * (size_t)quad_elems(g)) : 0);
+  L.wdt = L.xq + (use_quad(g) ? ws_align(2 * (size_t)quad_elems(g)) : 0);
+  L.total = L.wdt + ws_align(2 * (size_t)g.G * nkc * ((g.Cog + 63) / 64) * 4096);
   return L;
 }
 
@@ -480,10 +481,15 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   {
-    KernelScope ks("weight_swizzle", st);
-    const int nkc = (g.Cig / BK) * g.T;
-    const dim3 grid((unsigned)(g.G * nkc), (unsigned)((g.Cog * 8 + 255) / 256));
-    weight_swizzle_kernel<T><<<grid, 256, 0, st>>>(w, wsw, g.Cog, g.Cig, g.T, nkc);
+    // both weight images in one pass; training keeps dgrad's with the saved state
+    T* wdt = saved ? reinterpret_cast<T*>(static_cast<char*>(saved) + SV.wdt) : nullptr;
+    KernelScope ks("weight_images", st);
+    if (!weight_images_launch<T>(w, wsw, wdt, g, st)) {
+      const int nkc = (g.Cig / BK) * g.T;
+      const dim3 grid((unsigned)(g.G * nkc), (unsigned)((g.Cog * 8 + 255) / 256));
+      weight_swizzle_kernel<T><<<grid, 256, 0, st>>>(w, wsw, g.Cog, g.Cig, g.T, nkc);
+      if (wdt) weight_t_images(w, wdt, g, st);
+    }
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 

@@ -20,9 +20,15 @@ size_t tc_backward_workspace(const dcn_conv_desc& d, const Geom& g);
 //         shared-memory image, so the weight-gradient GEMM streams them back
 //         with bulk copies instead of gathering again.
 //   xq    corner-quad records of the input (offset groups of 8 channels)
+//   wdt   dgrad's W^T tile image of the weight (the backward does not
+//         rebuild it: the weight must not change between the two calls)
 struct SavedLayout {
-  size_t xh, cols, xq, total;
+  size_t xh, cols, xq, wdt, total;
 };
+
+// Host: dgrad's W^T tile image of the weight into wdt (dcn_tc_bwd.cu).
+template <typename T>
+void weight_t_images(const T* w, T* wdt, const Geom& g, cudaStream_t st);
 SavedLayout saved_layout(const Geom& g);
 
 // `saved` may be null (nothing kept / nothing available).

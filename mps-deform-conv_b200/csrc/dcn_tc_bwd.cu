@@ -1323,6 +1323,19 @@ __global__ void weight_t_swizzle_kernel(const T* __restrict__ w, T* __restrict__
   }
 }
 
+}  // namespace
+
+template <typename T>
+void weight_t_images(const T* w, T* wdt, const Geom& g, cudaStream_t st) {
+  const int nkc = (g.Cig / BK) * g.T, KB = (g.Cog + 63) / 64;
+  weight_t_swizzle_kernel<T><<<dim3((unsigned)(g.G * nkc), (unsigned)KB), 256, 0, st>>>(w, wdt, g.Cog, g.Cig, g.T,
+                                                                                        nkc);
+}
+template void weight_t_images<__half>(const __half*, __half*, const Geom&, cudaStream_t);
+template void weight_t_images<__nv_bfloat16>(const __nv_bfloat16*, __nv_bfloat16*, const Geom&, cudaStream_t);
+
+namespace {
+
 // channels-last fp32 [B][HW][C] -> NCHW T [B][C][HW].
 template <typename T>
 __global__ void nhwc_f32_to_nchw_kernel(const float* __restrict__ src, T* __restrict__ dst, int C, int HW) {
@@ -1675,10 +1688,11 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (need_d) {
-    {
-      KernelScope ks("weight_t_swizzle", st);
-      weight_t_swizzle_kernel<T><<<dim3((unsigned)(g.G * nkc), (unsigned)KB), 256, 0, st>>>(
-          w, wdt, g.Cog, g.Cig, g.T, nkc);
+    if (saved) {  // the forward built it with the training state
+      wdt = reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.wdt);
+    } else {
+      KernelScope ks("weight_images", st);
+      if (!weight_images_launch<T>(w, nullptr, wdt, g, st)) weight_t_images(w, wdt, g, st);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     DgradArgs a;

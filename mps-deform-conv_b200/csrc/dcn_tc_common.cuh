@@ -530,6 +530,80 @@ __device__ __forceinline__ bool gather_run_quad(const Geom& g, const T* __restri
   return true;
 }
 
+// ---------------------------------------------------------------- weight images
+// weight [Co][Cig][T] -> the two pre-swizzled tile images, in one pass: the
+// forward's wsw [G][NKC][Cog][64] (K chunk kc = t*(Cig/64) + cc, chunk q of
+// row co at q ^ (co % 8)) and dgrad's W^T tiles wdt [G][NKC][KB][64 ch][64 co]
+// (kc = cc*T + t, chunk q of row j at q ^ (j % 8), co >= Cog zero); either
+// output may be null.  blockIdx.x = 8 output channels (up to KB*64: the CTAs
+// past Cog write wdt's zero chunks), blockIdx.y = group, blockIdx.z = the
+// 64-channel block cc, whose T*64 weights of each output channel are
+// contiguous: the 8 rows' blocks are staged in shared memory with coalesced
+// loads, so every global access is a whole row run or a whole 16-byte chunk.
+// Dynamic shared memory: weight_images_smem(T) bytes.
+inline size_t weight_images_smem(int T_, size_t es) { return 8 * (size_t)BK * T_ * es; }
+
+template <typename T>
+__global__ void weight_images_kernel(const T* __restrict__ w, T* __restrict__ wsw, T* __restrict__ wdt, int Cog,
+                                     int Cig, int T_) {
+  extern __shared__ __align__(16) uint8_t wi_smem[];
+  T* rows = reinterpret_cast<T*>(wi_smem);  // [8][64 * T]: channels cc*64 .. cc*64+63 of 8 output channels
+  const int Kg = Cig * T_, ncc = Cig / BK, nkc = ncc * T_, KB = (Cog + 63) / 64, run = BK * T_;
+  const int grp = blockIdx.y, co0 = blockIdx.x * 8, cc = blockIdx.z;
+  const bool live = co0 < Cog;
+  {  // a row's run is 128*T bytes at a 128-byte multiple of w: 16-byte loads
+    const int run16 = run * (int)sizeof(T) / 16;
+    uint4* rows16 = reinterpret_cast<uint4*>(rows);
+    for (int i = threadIdx.x; i < 8 * run16; i += blockDim.x) {
+      const int r = i / run16, e = i - r * run16;
+      rows16[i] = live ? reinterpret_cast<const uint4*>(w + ((size_t)grp * Cog + co0 + r) * Kg +
+                                                        (size_t)cc * run)[e]
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  __syncthreads();
+  if (wsw && live) {  // (row r, tap t, chunk q) -> 16 bytes of row co0 + r of K chunk t*ncc + cc
+    for (int i = threadIdx.x; i < T_ * 64; i += blockDim.x) {
+      const int q = i & 7, rt = i >> 3, t = rt % T_, r = rt / T_;
+      const T* src = rows + r * run + (q * 8) * T_ + t;
+      __align__(16) T v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = src[j * T_];
+      const int co = co0 + r, kc = t * ncc + cc;
+      *reinterpret_cast<uint4*>(wsw + (((size_t)grp * nkc + kc) * Cog + co) * BK + ((q ^ (co & 7)) << 3)) =
+          *reinterpret_cast<const uint4*>(v);
+    }
+  }
+  if (wdt) {  // (tap t, channel row j) -> the chunk of output channels co0 .. co0+7 of K chunk cc*T + t
+    const int kb = co0 / 64, qq = (co0 % 64) / 8;
+    for (int i = threadIdx.x; i < T_ * 64; i += blockDim.x) {
+      const int j = i & 63, t = i >> 6;
+      __align__(16) T v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = rows[k * run + j * T_ + t];
+      const int kc = cc * T_ + t;
+      *reinterpret_cast<uint4*>(wdt + ((((size_t)grp * nkc + kc) * KB + kb) * 64 + j) * 64 + ((qq ^ (j & 7)) << 3)) =
+          *reinterpret_cast<const uint4*>(v);
+    }
+  }
+}
+
+// Launches weight_images_kernel; false when its staging does not fit (the
+// caller then uses the per-image kernels).
+template <typename T>
+inline bool weight_images_launch(const T* w, T* wsw, T* wdt, const Geom& g, cudaStream_t st) {
+  const size_t smem = weight_images_smem(g.T, sizeof(T));
+  if (smem > 96 * 1024 || (reinterpret_cast<uintptr_t>(w) & 15)) return false;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(weight_images_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return false;
+  const int KB = (g.Cog + 63) / 64;
+  weight_images_kernel<T><<<dim3((unsigned)(KB * 8), (unsigned)g.G, (unsigned)(g.Cig / BK)), 256, smem, st>>>(
+      w, wsw, wdt, g.Cog, g.Cig, g.T);
+  return true;
+}
+
 // ---------------------------------------------------------------- TMA (tensor)
 // 2-D tiled load (no multicast): box at (x = inner coordinate, y) of the
 // tensor described by `tmap` into shared memory at `dst`, completing as
