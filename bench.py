@@ -424,18 +424,20 @@ def run_suite(dev, skip, steps=5, warmup=3):
     """Short device-timed fwd(+bwd) runs of the other workloads (N=1): one
     entry per problem with ms/step, TFLOP/s, samples/s, which kernel family
     ran it and its top kernels.  Inputs stay resident; the L2 is flushed
-    between steps."""
+    between steps.  Forward-only problems on the tensor cores get a second
+    entry, "<name>/frozen_cl": the same call as a channels_last network in
+    inference makes it (input already channels_last, weights frozen, so the
+    forward weight image is built once: set_weight_image_cache)."""
     import mps_deform_conv as mdc
     from mps_deform_conv import _abi
     res = {}
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    for name, p in PROBLEMS.items():
-        if name == skip:
-            continue
-        inp = make_inputs(p, dev)
+
+    def measure(p, inp, channels_last=False):
         st, pd, dl = (p.stride,) * 2, (p.padding,) * 2, (p.dilation,) * 2
+        x = inp["input"].contiguous(memory_format=torch.channels_last) if channels_last else inp["input"]
         leaves = [t.requires_grad_(p.training) if t is not None else None
-                  for t in (inp["input"], inp["offset"], inp["weight"], inp["bias"], inp["mask"])]
+                  for t in (x, inp["offset"], inp["weight"], inp["bias"], inp["mask"])]
         lv = [t for t in leaves if t is not None]
 
         def step():
@@ -461,14 +463,28 @@ def run_suite(dev, skip, steps=5, warmup=3):
         tc = bool(mdc._get_lib().uses_tensor_cores(inp["input"], inp["weight"], p.stride, p.stride, p.padding,
                                                    p.padding, p.dilation, p.dilation, p.groups,
                                                    p.offset_groups, p.use_mask))
-        res[name] = {"description": p.description, "pass": "fwd+bwd" if p.training else "fwd",
-                     "ms_per_step": round(ms, 4), "tflops": round(p.flops() / (ms / 1e3) / 1e12, 3),
-                     "samples_per_s": round(p.batch / (ms / 1e3), 1),
-                     "min_hbm_bytes": p.min_hbm_bytes(),
-                     "hbm_frac_of_measured": round(p.min_hbm_bytes() / (ms / 1e3) / 1e9 / load_peaks()["hbm_gbs"], 4),
-                     "kernels": "tcgen05" if tc else "simt",
-                     "top": [{"name": n, "ms_per_step": round(t / steps, 4)} for n, l, t in prof[:3]]}
-        del inp, leaves, lv
+        return tc, {"description": p.description, "pass": "fwd+bwd" if p.training else "fwd",
+                    "ms_per_step": round(ms, 4), "tflops": round(p.flops() / (ms / 1e3) / 1e12, 3),
+                    "samples_per_s": round(p.batch / (ms / 1e3), 1),
+                    "min_hbm_bytes": p.min_hbm_bytes(),
+                    "hbm_frac_of_measured": round(p.min_hbm_bytes() / (ms / 1e3) / 1e9 / load_peaks()["hbm_gbs"], 4),
+                    "kernels": "tcgen05" if tc else "simt",
+                    "top": [{"name": n, "ms_per_step": round(t / steps, 4)} for n, l, t in prof[:3]]}
+
+    for name, p in PROBLEMS.items():
+        if name == skip:
+            continue
+        inp = make_inputs(p, dev)
+        tc, res[name] = measure(p, inp)
+        if tc and not p.training:
+            mdc.set_weight_image_cache(True)
+            try:
+                _, r = measure(p, inp, channels_last=True)
+            finally:
+                mdc.set_weight_image_cache(False)
+            r["description"] += "; channels_last input, frozen weights (cached weight image)"
+            res[name + "/frozen_cl"] = r
+        del inp
         torch.cuda.empty_cache()
     return res
 

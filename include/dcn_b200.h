@@ -275,9 +275,25 @@ typedef struct dcn_ex_options {
   int32_t input_layout;   /* input and grad_input */
   int32_t output_layout;  /* output and grad_output */
   int32_t head;           /* 1: offset is a DCNv2 head output [B][OG*T*3][Ho][Wo] */
-  int32_t reserved;       /* 0 */
+  int32_t flags;          /* 0, or DCN_EX_WEIGHT_IMAGE (forward only) */
 } dcn_ex_options;
+/* flags: `weight` is the forward weight image that dcn_weight_image built
+ * (forward calls without saved state, tensor-core problems only). */
+#define DCN_EX_WEIGHT_IMAGE 1
 DCN_API int dcn_ex_supported(const dcn_conv_desc *desc, const dcn_ex_options *opt, int backward);
+/* Forward weight image (no reference counterpart).  The tensor-core forward
+ * reads its weights as a pre-swizzled tile image [G][K chunks][Cog][64] that
+ * every call otherwise rebuilds from `weight`.  A caller whose weights do not
+ * change between forward-only calls (inference) builds it once:
+ * dcn_weight_image_bytes gives its size (as many elements as the weight; 0
+ * when the problem does not take the tensor-core forward), dcn_weight_image
+ * writes it (16-byte aligned) on `stream`, and dcn_deform_conv2d_forward_ex
+ * with flags = DCN_EX_WEIGHT_IMAGE and `weight` = the image skips the
+ * rebuild.  The image depends on the weight values, their dtype and the
+ * group split only; rebuild it after the weights change. */
+DCN_API size_t dcn_weight_image_bytes(const dcn_conv_desc *desc);
+DCN_API int dcn_weight_image(const dcn_conv_desc *desc, const void *weight, void *image, size_t image_bytes,
+                             void *stream);
 DCN_API int dcn_deform_conv2d_forward_ex(const dcn_conv_desc *desc, const dcn_ex_options *opt,
                                          const void *input, const void *weight, const void *offset,
                                          const void *mask, const void *bias, void *output, void *saved,
@@ -327,6 +343,31 @@ DCN_API int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc *desc, const 
  * it (it synchronises `stream`): DCN_OK, or DCN_ERR_DEVICE_TIMEOUT.
  */
 DCN_API int dcn_device_status(void *stream);
+
+/* ---------------------------------------------------------------------
+ * Bounds-checked build (no reference counterpart).  libdcn_b200_bounds.so,
+ * built from the same sources with -DDCN_DEBUG_BOUNDS, checks the gather and
+ * scatter index math of every kernel (corner, offset, mask, corner-quad
+ * record, grad_input and offset/mask-gradient element indices) against the
+ * extent of the tensor it addresses.  An index outside it is counted, the
+ * first one kept (site, index, element width of the access, extent), and
+ * the access redirected to element 0: the kernel neither traps nor stops.
+ * dcn_debug_bounds_enabled() is 1 in that build, 0 in the release library.
+ * dcn_debug_bounds_read synchronises the device, returns the record summed
+ * over the kernel files (all zero in the release library) and clears it when
+ * `reset` is non-zero.  Site codes: 1 bilinear corner, 2 coordinate-gradient
+ * corner, 3 tensor-core gather input vector, 4 offset element, 5 mask
+ * element, 6 corner-quad record, 7 dgrad corner vector, 8 dgrad grad_input
+ * reduction, 9 corner-quad reduction, 10 offset/mask gradient element,
+ * 11 SIMT col2im, 12 SIMT channels-last col2im, 13 SIMT im2col column.
+ */
+typedef struct dcn_bounds_record {
+  uint64_t count;         /* indices found outside their tensor */
+  int64_t index, extent;  /* the first one, and its tensor's element count */
+  int32_t site, width;    /* where it was computed; elements of the access */
+} dcn_bounds_record;
+DCN_API int dcn_debug_bounds_enabled(void);
+DCN_API int dcn_debug_bounds_read(dcn_bounds_record *out, int reset);
 
 /* Which implementation a descriptor runs on: 1 = tensor-core (tcgen05)
  * kernels, 0 = general SIMT kernels (any shape, fp32 path). */

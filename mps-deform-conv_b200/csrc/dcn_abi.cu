@@ -10,6 +10,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -50,6 +52,7 @@ static cudaEvent_t prof_event() {
 
 KernelScope::KernelScope(const char* name, cudaStream_t st) : name_(name), st_(st) {
   note_launch();
+  nvtxRangePushA(name);  // host-side range around the launch, named after the kernel
   if (!g_prof_on.load(std::memory_order_relaxed)) return;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
@@ -58,6 +61,7 @@ KernelScope::KernelScope(const char* name, cudaStream_t st) : name_(name), st_(s
 }
 
 KernelScope::~KernelScope() {
+  nvtxRangePop();
   if (!start_) return;
   cudaEvent_t stop = prof_event();
   if (!stop || cudaEventRecord(stop, st_) != cudaSuccess) return;
@@ -288,7 +292,7 @@ static int forward_impl(const dcn_conv_desc* d, const void* input, const void* w
     const size_t need_saved = saved ? saved_layout(g).total : 0;
     if (saved && saved_bytes < need_saved)
       return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", need_saved, saved_bytes);
-    cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, saved, st);
+    cudaError_t e = tc_forward(*d, g, input, weight, false, offset, mask, bias, output, workspace, saved, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward (tensor core)");
   }
   const size_t need = simt_forward_workspace(g);
@@ -517,7 +521,7 @@ int dcn_deform_conv2d_backward_overlap(const dcn_conv_desc* d, const void* grad_
 // sigmoid).  Anything but NCHW without the head needs the tensor-core path;
 // the head also needs 32-channel dgrad slabs.
 static bool plain_options(const dcn_ex_options* o) {
-  return !o || (o->input_layout == DCN_LAYOUT_NCHW && o->output_layout == DCN_LAYOUT_NCHW && !o->head);
+  return !o || (o->input_layout == DCN_LAYOUT_NCHW && o->output_layout == DCN_LAYOUT_NCHW && !o->head && !o->flags);
 }
 
 static Geom ex_geom(const dcn_conv_desc& d, const dcn_ex_options* o) {
@@ -536,13 +540,35 @@ int dcn_ex_supported(const dcn_conv_desc* d, const dcn_ex_options* o, int backwa
   if (validate(d) != DCN_OK) return 0;
   if (plain_options(o)) return 1;
   if ((o->input_layout != DCN_LAYOUT_NCHW && o->input_layout != DCN_LAYOUT_NHWC) ||
-      (o->output_layout != DCN_LAYOUT_NCHW && o->output_layout != DCN_LAYOUT_NHWC) || (o->head != 0 && o->head != 1))
+      (o->output_layout != DCN_LAYOUT_NCHW && o->output_layout != DCN_LAYOUT_NHWC) || (o->head != 0 && o->head != 1) ||
+      (o->flags & ~DCN_EX_WEIGHT_IMAGE) || ((o->flags & DCN_EX_WEIGHT_IMAGE) && backward))
     return 0;
   const Geom g = ex_geom(*d, o);
   if (o->head && (!d->use_mask || g.cpo % 32 != 0 || (long long)g.B * g.H * g.W * g.C >= (1LL << 31) ||
                   !tc_backward_supported(*d, g)))
     return 0;
   return (backward ? tc_backward_supported(*d, g) : tc_forward_supported(*d, g)) ? 1 : 0;
+}
+
+size_t dcn_weight_image_bytes(const dcn_conv_desc* d) {
+  const dcn_ex_options o = {DCN_LAYOUT_NCHW, DCN_LAYOUT_NCHW, 0, DCN_EX_WEIGHT_IMAGE};
+  if (!dcn_ex_supported(d, &o, 0)) return 0;
+  return elem_size(d->dtype) * (size_t)d->out_channels * (size_t)(d->in_channels / d->n_weight_grps) *
+         (size_t)(d->kernel_h * d->kernel_w);
+}
+
+int dcn_weight_image(const dcn_conv_desc* d, const void* weight, void* image, size_t image_bytes, void* stream) {
+  const size_t need = dcn_weight_image_bytes(d);
+  if (!need)
+    return fail(DCN_ERR_UNSUPPORTED, "weight_image: the problem does not run on the tensor-core forward");
+  if (!weight || !image) return fail(DCN_ERR_INVALID_ARGUMENT, "weight_image: NULL weight or image");
+  if (image_bytes < need)
+    return fail(DCN_ERR_WORKSPACE, "weight image too small: need %zu bytes, got %zu", need, image_bytes);
+  if ((reinterpret_cast<uintptr_t>(image) & 15) != 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "the weight image must be 16-byte aligned");
+  const Geom g = make_geom(*d);
+  cudaError_t e = tc_weight_image(*d, g, weight, image, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "weight_image");
 }
 
 int dcn_head_supported(const dcn_conv_desc* d) {
@@ -555,9 +581,9 @@ static int ex_check(const dcn_conv_desc* d, const dcn_ex_options* o, int backwar
   if (r != DCN_OK) return r;
   if (!dcn_ex_supported(d, o, backward))
     return fail(DCN_ERR_UNSUPPORTED,
-                "%s: channels-last layouts and the DCNv2 head layout need fp16/bf16 with per-group channels that "
-                "the tensor-core kernels take (the head layout also needs use_mask and offset groups of a "
-                "multiple of 32 channels)",
+                "%s: channels-last layouts, the DCNv2 head layout and weight images need fp16/bf16 with "
+                "per-group channels that the tensor-core kernels take (the head layout also needs use_mask and "
+                "offset groups of a multiple of 32 channels; a weight image serves forward calls only)",
                 fn);
   return DCN_OK;
 }
@@ -586,9 +612,14 @@ int dcn_deform_conv2d_forward_ex(const dcn_conv_desc* d, const dcn_ex_options* o
   if (saved && saved_bytes < saved_layout(g).total)
     return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", saved_layout(g).total,
                 saved_bytes);
+  const bool image = (o->flags & DCN_EX_WEIGHT_IMAGE) != 0;
+  if (image && saved)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "a weight image serves forward-only calls: saved must be NULL");
+  if (image && !aligned16(weight))
+    return fail(DCN_ERR_INVALID_ARGUMENT, "the weight image must be 16-byte aligned");
   if (o->head)
     mask = static_cast<const char*>(offset) + elem_size(d->dtype) * (size_t)2 * g.OG * g.T * g.HWo;
-  cudaError_t e = tc_forward(*d, g, input, weight, offset, mask, bias, output, workspace, saved,
+  cudaError_t e = tc_forward(*d, g, input, weight, image, offset, mask, bias, output, workspace, saved,
                              (cudaStream_t)stream);
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward_ex");
 }
@@ -686,6 +717,30 @@ int dcn_deform_conv2d_backward_input_noalloc(const dcn_conv_desc* d0, const void
                                                   dd.use_mask ? mask : nullptr, grad_input,
                                                   (cudaStream_t)stream);
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_backward_input_noalloc");
+}
+
+int dcn_debug_bounds_enabled(void) {
+#ifdef DCN_DEBUG_BOUNDS
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+int dcn_debug_bounds_read(dcn_bounds_record* out, int reset) {
+  if (!out) return fail(DCN_ERR_INVALID_ARGUMENT, "dcn_debug_bounds_read: out is NULL");
+  dcn::DebugBounds acc = {};
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = dcn::debug_bounds_collect_tc(&acc, reset != 0);
+  if (e == cudaSuccess) e = dcn::debug_bounds_collect_tc_bwd(&acc, reset != 0);
+  if (e == cudaSuccess) e = dcn::debug_bounds_collect_simt(&acc, reset != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "dcn_debug_bounds_read");
+  out->count = acc.count;
+  out->index = acc.index;
+  out->extent = acc.extent;
+  out->site = acc.site;
+  out->width = acc.width;
+  return ok();
 }
 
 int dcn_device_status(void* stream) {

@@ -15,6 +15,7 @@
 #include <stdint.h>
 
 #include "dcn_b200.h"
+#include "dcn_debug.cuh"
 
 namespace dcn {
 
@@ -146,10 +147,10 @@ __device__ __forceinline__ Corners corners_of(const SamplePos& s, int H, int W) 
   c.w[1] = (vy0 && vx1) ? hy * lx : 0.0f;
   c.w[2] = (vy1 && vx0) ? ly * hx : 0.0f;
   c.w[3] = (vy1 && vx1) ? ly * lx : 0.0f;
-  c.idx[0] = (vy0 && vx0) ? y0 * W + x0 : 0;
-  c.idx[1] = (vy0 && vx1) ? y0 * W + x1 : 0;
-  c.idx[2] = (vy1 && vx0) ? y1 * W + x0 : 0;
-  c.idx[3] = (vy1 && vx1) ? y1 * W + x1 : 0;
+  c.idx[0] = (vy0 && vx0) ? DCN_BOUND(y0 * W + x0, 1, (long long)H * W, DBG_CORNER) : 0;
+  c.idx[1] = (vy0 && vx1) ? DCN_BOUND(y0 * W + x1, 1, (long long)H * W, DBG_CORNER) : 0;
+  c.idx[2] = (vy1 && vx0) ? DCN_BOUND(y1 * W + x0, 1, (long long)H * W, DBG_CORNER) : 0;
+  c.idx[3] = (vy1 && vx1) ? DCN_BOUND(y1 * W + x1, 1, (long long)H * W, DBG_CORNER) : 0;
   return c;
 }
 
@@ -176,10 +177,10 @@ __device__ __forceinline__ CoordCorners coord_corners_of(const SamplePos& s, int
   const bool vy0 = 0 <= y0 && y0 < H, vy1 = 0 <= y1 && y1 < H;
   const bool vx0 = 0 <= x0 && x0 < W, vx1 = 0 <= x1 && x1 < W;
   c.v[0] = vy0 && vx0; c.v[1] = vy0 && vx1; c.v[2] = vy1 && vx0; c.v[3] = vy1 && vx1;
-  c.idx[0] = c.v[0] ? y0 * W + x0 : 0;
-  c.idx[1] = c.v[1] ? y0 * W + x1 : 0;
-  c.idx[2] = c.v[2] ? y1 * W + x0 : 0;
-  c.idx[3] = c.v[3] ? y1 * W + x1 : 0;
+  c.idx[0] = c.v[0] ? DCN_BOUND(y0 * W + x0, 1, (long long)H * W, DBG_COORD_CORNER) : 0;
+  c.idx[1] = c.v[1] ? DCN_BOUND(y0 * W + x1, 1, (long long)H * W, DBG_COORD_CORNER) : 0;
+  c.idx[2] = c.v[2] ? DCN_BOUND(y1 * W + x0, 1, (long long)H * W, DBG_COORD_CORNER) : 0;
+  c.idx[3] = c.v[3] ? DCN_BOUND(y1 * W + x1, 1, (long long)H * W, DBG_COORD_CORNER) : 0;
   return c;
 }
 

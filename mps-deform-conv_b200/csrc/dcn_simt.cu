@@ -309,7 +309,9 @@ __global__ void im2col_og_kernel(Geom g, const T* __restrict__ x, const T* __res
     const Corners cs = corners_of(sp, g.H, g.W);
     const T* src = x + ((long long)b * g.C + (long long)o * g.cpo) * plane;
     TC* dst = cols + ((long long)o * g.cpo * g.T + t) * g.P + n;
-    for (int c = 0; c < g.cpo; ++c) dst[(long long)c * row_stride] = from_f<TC>(m * bilinear(src + (long long)c * plane, cs));
+    for (int c = 0; c < g.cpo; ++c)
+      dst[DCN_BOUND((long long)c * row_stride, 1, (long long)g.C * g.T * g.P - (dst - cols), DBG_SIMT_IM2COL)] =
+          from_f<TC>(m * bilinear(src + (long long)c * plane, cs));
   }
 }
 
@@ -327,10 +329,12 @@ __global__ void col2im_kernel(Geom g, const TC* __restrict__ gcol, const T* __re
     const SamplePos sp = sample_point(g, off, msk, b, c / g.cpo, t, p, &m);
     const Corners cs = corners_of(sp, g.H, g.W);
     const float v = m * to_f(gcol[e]);
-    float* plane = gin + ((long long)b * g.C + c) * g.H * g.W;
 #pragma unroll
     for (int k = 0; k < 4; ++k)
-      if (cs.w[k] != 0.0f) atomicAdd(plane + cs.idx[k], cs.w[k] * v);
+      if (cs.w[k] != 0.0f)
+        atomicAdd(gin + DCN_BOUND(((long long)b * g.C + c) * g.H * g.W + cs.idx[k], 1, (long long)g.B * g.C * g.H * g.W,
+                                  DBG_SIMT_COL2IM),
+                  cs.w[k] * v);
   }
 }
 
@@ -360,11 +364,13 @@ __global__ void col2im_nhwc4_kernel(Geom g, const TC* __restrict__ gcol, const T
     const long long rs = (long long)g.T * g.P;  // channel c -> c + 1 in the column layout
     const TC* src = gcol + ((long long)c * g.T + t) * g.P + n;
     const float v0 = m * to_f(src[0]), v1 = m * to_f(src[rs]), v2 = m * to_f(src[2 * rs]), v3 = m * to_f(src[3 * rs]);
-    float* base = acc + (long long)b * g.H * g.W * g.C + c;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float w = cs.w[k];
-      if (w != 0.0f) red_add_v4(base + (long long)cs.idx[k] * g.C, w * v0, w * v1, w * v2, w * v3);
+      if (w != 0.0f)
+        red_add_v4(acc + DCN_BOUND(((long long)b * g.H * g.W + cs.idx[k]) * g.C + c, 4, (long long)g.B * g.H * g.W * g.C,
+                                   DBG_SIMT_COL2IM_NHWC),
+                   w * v0, w * v1, w * v2, w * v3);
     }
   }
 }
@@ -681,5 +687,7 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
 DCN_SIMT_INSTANCES(float)
 DCN_SIMT_INSTANCES(__half)
 DCN_SIMT_INSTANCES(__nv_bfloat16)
+
+DCN_DEBUG_BOUNDS_TU(simt)
 
 }  // namespace dcn

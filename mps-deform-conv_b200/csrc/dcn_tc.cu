@@ -459,16 +459,32 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, 
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Forward weight image wsw of `w` (weight_images_kernel, or the per-image
+// kernel when its staging does not fit).
 template <typename T>
-static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
-                                const T* bias, T* out, void* workspace, void* saved, cudaStream_t st) {
+static void forward_weight_image(const T* w, T* wsw, T* wdt, const Geom& g, cudaStream_t st) {
+  KernelScope ks("weight_images", st);
+  if (!weight_images_launch<T>(w, wsw, wdt, g, st)) {
+    const int nkc = (g.Cig / BK) * g.T;
+    const dim3 grid((unsigned)(g.G * nkc), (unsigned)((g.Cog * 8 + 255) / 256));
+    weight_swizzle_kernel<T><<<grid, 256, 0, st>>>(w, wsw, g.Cog, g.Cig, g.T, nkc);
+    if (wdt) weight_t_images(w, wdt, g, st);
+  }
+}
+
+// w_is_image: `w` is already the forward weight image (tc_weight_image), and
+// nothing is saved.
+template <typename T>
+static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, bool w_is_image, const T* off,
+                                const T* msk, const T* bias, T* out, void* workspace, void* saved,
+                                cudaStream_t st) {
   const FwdWs L = fwd_ws(g, sizeof(T));
   const SavedLayout SV = saved_layout(g);
   // channels-last input: the gather reads it directly; else a channels-last copy
   T* xh = g.in_nhwc ? const_cast<T*>(x)
                     : reinterpret_cast<T*>(saved ? static_cast<char*>(saved) + SV.xh
                                                  : static_cast<char*>(workspace) + L.xh);
-  T* wsw = reinterpret_cast<T*>(static_cast<char*>(workspace) + L.wsw);
+  T* wsw = w_is_image ? const_cast<T*>(w) : reinterpret_cast<T*>(static_cast<char*>(workspace) + L.wsw);
   cudaError_t e;
   if (!g.in_nhwc) {
     KernelScope ks("nchw_to_nhwc", st);
@@ -480,18 +496,12 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
       nchw_to_nhwc_kernel<T><<<grid, 256, 0, st>>>(x, xh, g.C, g.H * g.W);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  {
+  if (!w_is_image) {
     // both weight images in one pass; training keeps dgrad's with the saved state
     T* wdt = saved ? reinterpret_cast<T*>(static_cast<char*>(saved) + SV.wdt) : nullptr;
-    KernelScope ks("weight_images", st);
-    if (!weight_images_launch<T>(w, wsw, wdt, g, st)) {
-      const int nkc = (g.Cig / BK) * g.T;
-      const dim3 grid((unsigned)(g.G * nkc), (unsigned)((g.Cog * 8 + 255) / 256));
-      weight_swizzle_kernel<T><<<grid, 256, 0, st>>>(w, wsw, g.Cog, g.Cig, g.T, nkc);
-      if (wdt) weight_t_images(w, wdt, g, st);
-    }
+    forward_weight_image(w, wsw, wdt, g, st);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   const bool quad = use_quad(g) && (reinterpret_cast<uintptr_t>(xh) & 15) == 0;
   // training: the records stay with the saved state for the backward's corner reads
@@ -535,16 +545,24 @@ static cudaError_t tc_forward_t(const Geom& g, const T* x, const T* w, const T* 
 }
 
 cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
-                       const void* offset, const void* mask, const void* bias, void* output,
-                       void* workspace, void* saved, cudaStream_t st) {
+                       bool weight_is_image, const void* offset, const void* mask, const void* bias,
+                       void* output, void* workspace, void* saved, cudaStream_t st) {
   if (d.dtype == DCN_BFLOAT16)
     return tc_forward_t<__nv_bfloat16>(g, (const __nv_bfloat16*)input, (const __nv_bfloat16*)weight,
-                                       (const __nv_bfloat16*)offset, (const __nv_bfloat16*)mask,
-                                       (const __nv_bfloat16*)bias, (__nv_bfloat16*)output, workspace,
-                                       saved, st);
-  return tc_forward_t<__half>(g, (const __half*)input, (const __half*)weight, (const __half*)offset,
-                              (const __half*)mask, (const __half*)bias, (__half*)output, workspace,
-                              saved, st);
+                                       weight_is_image, (const __nv_bfloat16*)offset, (const __nv_bfloat16*)mask,
+                                       (const __nv_bfloat16*)bias, (__nv_bfloat16*)output, workspace, saved, st);
+  return tc_forward_t<__half>(g, (const __half*)input, (const __half*)weight, weight_is_image,
+                              (const __half*)offset, (const __half*)mask, (const __half*)bias, (__half*)output,
+                              workspace, saved, st);
+}
+
+cudaError_t tc_weight_image(const dcn_conv_desc& d, const Geom& g, const void* weight, void* image,
+                            cudaStream_t st) {
+  if (d.dtype == DCN_BFLOAT16)
+    forward_weight_image((const __nv_bfloat16*)weight, (__nv_bfloat16*)image, (__nv_bfloat16*)nullptr, g, st);
+  else
+    forward_weight_image((const __half*)weight, (__half*)image, (__half*)nullptr, g, st);
+  return cudaGetLastError();
 }
 
 
@@ -556,5 +574,7 @@ cudaError_t tc_read_and_clear_status(int* out, cudaStream_t st) {
   const int zero = 0;
   return cudaMemcpyToSymbol(sm100::g_dcn_status, &zero, sizeof(int));
 }
+
+DCN_DEBUG_BOUNDS_TU(tc)
 
 }  // namespace dcn

@@ -31,10 +31,15 @@ template <typename T>
 void weight_t_images(const T* w, T* wdt, const Geom& g, cudaStream_t st);
 SavedLayout saved_layout(const Geom& g);
 
-// `saved` may be null (nothing kept / nothing available).
+// `saved` may be null (nothing kept / nothing available).  weight_is_image:
+// `weight` is the forward weight image from tc_weight_image (saved null).
 cudaError_t tc_forward(const dcn_conv_desc& d, const Geom& g, const void* input, const void* weight,
-                       const void* offset, const void* mask, const void* bias, void* output,
-                       void* workspace, void* saved, cudaStream_t st);
+                       bool weight_is_image, const void* offset, const void* mask, const void* bias,
+                       void* output, void* workspace, void* saved, cudaStream_t st);
+// The forward weight image [G][NKC][Cog][64] (pre-swizzled rows) of `weight`,
+// as many elements as the weight.
+cudaError_t tc_weight_image(const dcn_conv_desc& d, const Geom& g, const void* weight, void* image,
+                            cudaStream_t st);
 cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_output,
                         const void* input, const void* weight, const void* offset, const void* mask,
                         const void* saved, void* grad_input, void* grad_weight, void* grad_offset,

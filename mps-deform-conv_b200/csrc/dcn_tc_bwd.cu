@@ -654,7 +654,9 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         uint4 xv[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint4*>(xh + (cof[k] + cl))) : make_uint4(0, 0, 0, 0);
+          xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint4*>(
+                                       xh + DCN_BOUND(cof[k] + cl, 8, (long long)g.B * g.H * g.W * g.C, DBG_DG_CORNER_X)))
+                                 : make_uint4(0, 0, 0, 0);
         const float2 g01 = Vec<T>::unpack(gd.x), g23 = Vec<T>::unpack(gd.y), g45 = Vec<T>::unpack(gd.z),
                      g67 = Vec<T>::unpack(gd.w);
         float d[4];
@@ -674,8 +676,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         for (int k = 0; k < 4; ++k) {
           const float wk = w[k] * m;
           if (wk != 0.f) {
-            red_v4(a.gi32 + (cof[k] + cr0), wk * r01.x, wk * r01.y, wk * r23.x, wk * r23.y);
-            red_v4(a.gi32 + (cof[k] + cr1), wk * r45.x, wk * r45.y, wk * r67.x, wk * r67.y);
+            red_v4(a.gi32 + DCN_BOUND(cof[k] + cr0, 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_SCATTER), wk * r01.x, wk * r01.y, wk * r23.x,
+                   wk * r23.y);
+            red_v4(a.gi32 + DCN_BOUND(cof[k] + cr1, 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_SCATTER), wk * r45.x, wk * r45.y, wk * r67.x,
+                   wk * r67.y);
           }
         }
         __syncwarp();  // every lane has read this step's rows: the consumed chunks take the partial sums
@@ -694,11 +698,13 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           gm += pv.z;
         }
         if (pc.valid) {
-          const long long ob = (long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          const long long ob = DCN_BOUND((long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p,
+                                         g.HWo + 1, g.B * g.off_bs, DBG_DG_COORD);
           atomicAdd(a.goff32 + ob, gy);
           atomicAdd(a.goff32 + ob + g.HWo, gx);
           if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
-            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + pc.p,
+            atomicAdd(a.gmsk32 + DCN_BOUND((long long)pc.b * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + pc.p, 1,
+                                           g.B * g.msk_bs, DBG_DG_COORD),
                       g.msk_logit ? gm * tab_m * (1.f - tab_m) : gm);
         }
       }
@@ -772,10 +778,12 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       auto load_sample = [&](int row, T& dy, T& dx, T& mr) {
         const int4 p4 = ws->pix[row];
         if (p4.x >= 0) {
-          const long long ob = (long long)p4.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + p4.y;
+          const long long ob = DCN_BOUND((long long)p4.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + p4.y,
+                                         g.HWo + 1, g.B * g.off_bs, DBG_TC_GATHER_OFF);
           dy = off[ob];
           dx = off[ob + g.HWo];
-          mr = g.use_mask ? msk[(long long)p4.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + p4.y]
+          mr = g.use_mask ? msk[DCN_BOUND((long long)p4.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + p4.y, 1,
+                                          g.B * g.msk_bs, DBG_TC_GATHER_MSK)]
                           : from_f<T>(1.f);
         }
       };
@@ -798,7 +806,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         int rec = -1;
         float wm[4] = {0.f, 0.f, 0.f, 0.f};
         if (px.x >= 0) {
-          const long long ob = (long long)px.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + px.y;
+          const long long ob = DCN_BOUND((long long)px.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + px.y,
+                                         g.HWo + 1, g.B * g.off_bs, DBG_DG_COORD);
           const float dy = to_f(cdy), dx = to_f(cdx);
           const float m = g.use_mask ? mask_of(g, to_f(cmr)) : 1.f;
           const SamplePos sp = sample_pos(px.z + kw.ti * g.dh, px.w + kw.tj * g.dw, dy, dx);
@@ -809,7 +818,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
                          make_uint4(0, 0, 0, 0)};
           if (sp.y0 >= -1 && sp.y0 < g.H && sp.x0 >= -1 && sp.x0 < g.W) {
             rec = ((px.x * (g.H + 1) + sp.y0 + 1) * W1 + sp.x0 + 1) * OG + o;
-            const T* r = xq + (uint32_t)rec * 32u;
+            const T* r = xq + DCN_BOUND((uint32_t)rec * 32u, 32, quad_elems(g), DBG_TC_GATHER_QUAD);
             ldg256(r, xv[0], xv[1]);
             ldg256(r + 16, xv[2], xv[3]);
           }
@@ -832,7 +841,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
             go_[ob + g.HWo] = from_f<T>(gx);
           }
           if (a.gmsk_t)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
-            static_cast<T*>(a.gmsk_t)[(long long)px.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + px.y] =
+            static_cast<T*>(a.gmsk_t)[DCN_BOUND((long long)px.x * g.msk_bs + (long long)(o * g.T + kw.t) * g.HWo + px.y,
+                                                1, g.B * g.msk_bs, DBG_DG_COORD)] =
                 from_f<T>(g.msk_logit ? gm * m * (1.f - m) : gm);
 #pragma unroll
           for (int k = 0; k < 4; ++k) wm[k] = cs.w[k] * m;
@@ -860,7 +870,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
             const int rs = ws->rec[src];
             if (rs >= 0) {
               const float4 v = *reinterpret_cast<const float4*>(ws->stage[src] + 4 * (j8 ^ (src & 7)));
-              red_v4(a.gq32 + (uint32_t)rs * 32u + 4 * j8, v.x, v.y, v.z, v.w);
+              red_v4(a.gq32 + DCN_BOUND((uint32_t)rs * 32u + 4 * j8, 4, quad_elems(g), DBG_DG_QUAD_SCATTER), v.x, v.y,
+                     v.z, v.w);
             }
           }
           __syncwarp();  // the staging area is rewritten by the next step
@@ -901,11 +912,14 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       float run_gy = 0.f, run_gx = 0.f, run_gm = 0.f;
       auto flush = [&]() {
         if (acc_o >= 0 && pc.valid) {
-          const long long ob = (long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          const long long ob =
+              DCN_BOUND((long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p,
+                        g.HWo + 1, g.B * g.off_bs, DBG_DG_COORD);
           atomicAdd(a.goff32 + ob, run_gy);
           atomicAdd(a.goff32 + ob + g.HWo, run_gx);
           if (g.use_mask)  // d/dlogit = m (1 - m) d/dm for a mask stored as logits
-            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p,
+            atomicAdd(a.gmsk32 + DCN_BOUND((long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p,
+                                           1, g.B * g.msk_bs, DBG_DG_COORD),
                       g.msk_logit ? run_gm * acc_m * (1.f - acc_m) : run_gm);
         }
         run_gy = run_gx = run_gm = 0.f;
@@ -983,7 +997,9 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           uint2 xv[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + eo[k])) : make_uint2(0, 0);
+            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(
+                                         xh + DCN_BOUND(eo[k], 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_CORNER_X)))
+                                   : make_uint2(0, 0);
           // d[k] = sum over the lane's 4 channels of gcol * x at corner k; the
           // mask, offset-y and offset-x partial sums are linear in them
           float d[4];
@@ -998,7 +1014,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float wk = w[k] * m;
-            if (wk != 0.f) red_v4(a.gi32 + eo[k], wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
+            if (wk != 0.f)
+              red_v4(a.gi32 + DCN_BOUND(eo[k], 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_SCATTER), wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
           }
           // the lane's partial sums replace the slab chunk it alone has read
           *reinterpret_cast<float4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2)) = make_float4(pgy, pgx, pgm, 0.f);
@@ -1058,11 +1075,14 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
       // mask holds logits, runs on the 32-channel variant only)
       auto flush = [&]() {
         if (acc_o >= 0 && pc.valid) {
-          const long long ob = (long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p;
+          const long long ob =
+              DCN_BOUND((long long)pc.b * g.off_bs + (long long)(acc_o * 2 * g.T + 2 * kw.t) * g.HWo + pc.p,
+                        g.HWo + 1, g.B * g.off_bs, DBG_DG_COORD);
           atomicAdd(a.goff32 + ob, run_gy);
           atomicAdd(a.goff32 + ob + g.HWo, run_gx);
           if (g.use_mask)
-            atomicAdd(a.gmsk32 + (long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p, run_gm);
+            atomicAdd(a.gmsk32 + DCN_BOUND((long long)pc.b * g.msk_bs + (long long)(acc_o * g.T + kw.t) * g.HWo + pc.p,
+                                           1, g.B * g.msk_bs, DBG_DG_COORD), run_gm);
         }
         run_gy = run_gx = run_gm = 0.f;
       };
@@ -1135,7 +1155,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           uint2 xv[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(xh + (long long)ci[k] * g.C + c_abs))
+            xv[k] = (cv >> k & 1u) ? __ldg(reinterpret_cast<const uint2*>(
+                                         xh + DCN_BOUND((long long)ci[k] * g.C + c_abs, 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_CORNER_X)))
                                    : make_uint2(0, 0);
           float d[4];  // per corner: sum over the lane's 4 channels of gcol * x
 #pragma unroll
@@ -1150,7 +1171,8 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           for (int k = 0; k < 4; ++k) {
             const float wk = w[k] * m;
             if (wk != 0.f)
-              red_v4(a.gi32 + (long long)ci[k] * g.C + c_abs, wk * gv.x, wk * gv.y, wk * gv.z, wk * gv.w);
+              red_v4(a.gi32 + DCN_BOUND((long long)ci[k] * g.C + c_abs, 4, (long long)g.B * g.H * g.W * g.C, DBG_DG_SCATTER), wk * gv.x,
+                     wk * gv.y, wk * gv.z, wk * gv.w);
           }
           pgy += __shfl_xor_sync(0xffffffffu, pgy, 1);
           pgx += __shfl_xor_sync(0xffffffffu, pgx, 1);
@@ -1825,5 +1847,7 @@ cudaError_t tc_backward(const dcn_conv_desc& d, const Geom& g, const void* grad_
                           (const T*)mask, saved, (T*)grad_input, (T*)grad_weight, (T*)grad_offset,
                           (T*)grad_mask, (T*)grad_bias, workspace, st, ready, user);
 }
+
+DCN_DEBUG_BOUNDS_TU(tc_bwd)
 
 }  // namespace dcn

@@ -88,10 +88,13 @@ __device__ __forceinline__ RawSample<T> load_raw(const Geom& g, const T* __restr
                                                  const T* __restrict__ msk, const PixelCtx& pc, int o,
                                                  int t) {
   RawSample<T> r;
-  const long long ob = (long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * t) * g.HWo + pc.p;
+  const long long ob = DCN_BOUND((long long)pc.b * g.off_bs + (long long)(o * 2 * g.T + 2 * t) * g.HWo + pc.p,
+                                 g.HWo + 1, g.B * g.off_bs, DBG_TC_GATHER_OFF);
   r.dy = off[ob];
   r.dx = off[ob + g.HWo];
-  r.m = msk ? msk[(long long)pc.b * g.msk_bs + (long long)(o * g.T + t) * g.HWo + pc.p] : from_f<T>(1.f);
+  r.m = msk ? msk[DCN_BOUND((long long)pc.b * g.msk_bs + (long long)(o * g.T + t) * g.HWo + pc.p, 1,
+                            g.B * g.msk_bs, DBG_TC_GATHER_MSK)]
+            : from_f<T>(1.f);
   return r;
 }
 
@@ -245,10 +248,11 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
   }
   auto load = [&](int h, int o, int t) {
     RawSample<T> rs;
-    const int ob = oo[h] + (o * 2 * g.T + 2 * t) * g.HWo;
+    const int ob = DCN_BOUND(oo[h] + (o * 2 * g.T + 2 * t) * g.HWo, g.HWo + 1, g.B * g.off_bs, DBG_TC_GATHER_OFF);
     rs.dy = off[ob];
     rs.dx = off[ob + g.HWo];
-    rs.m = msk ? msk[mo[h] + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    rs.m = msk ? msk[DCN_BOUND(mo[h] + (o * g.T + t) * g.HWo, 1, g.B * g.msk_bs, DBG_TC_GATHER_MSK)]
+               : from_f<T>(1.f);
     return rs;
   };
   GatherWalk kw;
@@ -274,7 +278,9 @@ __device__ __forceinline__ bool gather_run(const Geom& g, const T* __restrict__ 
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         v[h][k] = (cs[h].w[k] != 0.f)
-                      ? __ldg(reinterpret_cast<const uint4*>(xh + (uint32_t)(xo[h] + cs[h].off[k] + c0)))
+                      ? __ldg(reinterpret_cast<const uint4*>(
+                            xh + DCN_BOUND((uint32_t)(xo[h] + cs[h].off[k] + c0), 8,
+                                           (long long)g.B * g.H * g.W * g.C, DBG_TC_GATHER_X)))
                       : make_uint4(0, 0, 0, 0);
     // the next chunk: same sampling points, or prefetch their offsets and masks
     if (i + 1 < nk) {
@@ -327,10 +333,11 @@ __device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restri
   const int og0 = cbase_grp / g.cpo;  // offset group of the weight group's first channel chunk
   auto load = [&](int o, int t) {
     RawSample<T> rs;
-    const int ob = oo + (o * 2 * g.T + 2 * t) * g.HWo;
+    const int ob = DCN_BOUND(oo + (o * 2 * g.T + 2 * t) * g.HWo, g.HWo + 1, g.B * g.off_bs, DBG_TC_GATHER_OFF);
     rs.dy = off[ob];
     rs.dx = off[ob + g.HWo];
-    rs.m = msk ? msk[mo + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    rs.m = msk ? msk[DCN_BOUND(mo + (o * g.T + t) * g.HWo, 1, g.B * g.msk_bs, DBG_TC_GATHER_MSK)]
+               : from_f<T>(1.f);
     return rs;
   };
   // chunk position in gather order: tap t = (ti, tj), channel chunk cc, its
@@ -365,7 +372,8 @@ __device__ __forceinline__ bool gather_run_wide(const Geom& g, const T* __restri
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       if (c.w[k] != 0.f) {
-        const uint4* src = reinterpret_cast<const uint4*>(xh + (uint32_t)(xo + c.off[k] + cb));
+        const uint4* src = reinterpret_cast<const uint4*>(
+            xh + DCN_BOUND((uint32_t)(xo + c.off[k] + cb), 40, (long long)g.B * g.H * g.W * g.C, DBG_TC_GATHER_X));
         dst[2 * k] = __ldg(src);
         dst[2 * k + 1] = __ldg(src + 4);  // 32 channels further
       } else {
@@ -476,10 +484,11 @@ __device__ __forceinline__ bool gather_run_quad(const Geom& g, const T* __restri
   }
   auto load = [&](int h, int o, int t) {
     RawSample<T> rs;
-    const int ob = oo[h] + (o * 2 * g.T + 2 * t) * g.HWo;
+    const int ob = DCN_BOUND(oo[h] + (o * 2 * g.T + 2 * t) * g.HWo, g.HWo + 1, g.B * g.off_bs, DBG_TC_GATHER_OFF);
     rs.dy = off[ob];
     rs.dx = off[ob + g.HWo];
-    rs.m = msk ? msk[mo[h] + (o * g.T + t) * g.HWo] : from_f<T>(1.f);
+    rs.m = msk ? msk[DCN_BOUND(mo[h] + (o * g.T + t) * g.HWo, 1, g.B * g.msk_bs, DBG_TC_GATHER_MSK)]
+               : from_f<T>(1.f);
     return rs;
   };
   GatherWalk kw;
@@ -502,7 +511,8 @@ __device__ __forceinline__ bool gather_run_quad(const Geom& g, const T* __restri
       for (int k = 0; k < 4; ++k) w[h][k] = c.w[k] * m;
       // a non-zero weight implies the sample lies inside (-1, H) x (-1, W)
       if (w[h][0] != 0.f || w[h][1] != 0.f || w[h][2] != 0.f || w[h][3] != 0.f) {
-        const T* rec = xq + (uint32_t)(((qb[h] + sp.y0 + 1) * (g.W + 1) + sp.x0 + 1) * (g.C * 4) + o * 32);
+        const T* rec = xq + DCN_BOUND((uint32_t)(((qb[h] + sp.y0 + 1) * (g.W + 1) + sp.x0 + 1) * (g.C * 4) + o * 32),
+                                      32, quad_elems(g), DBG_TC_GATHER_QUAD);
         ldg256(rec, v[h][0], v[h][1]);
         ldg256(rec + 16, v[h][2], v[h][3]);
       } else {

@@ -115,7 +115,7 @@ dcn_ex_options ex_options(bool in_nhwc, bool out_nhwc, bool head) {
   o.input_layout = in_nhwc ? DCN_LAYOUT_NHWC : DCN_LAYOUT_NCHW;
   o.output_layout = out_nhwc ? DCN_LAYOUT_NHWC : DCN_LAYOUT_NCHW;
   o.head = head ? 1 : 0;
-  o.reserved = 0;
+  o.flags = 0;
   return o;
 }
 
@@ -198,15 +198,37 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_train(
   return {out, saved};
 }
 
+// Forward weight image of `weight` for this problem (dcn_weight_image), or an
+// empty tensor when the problem does not take the tensor-core forward.
+at::Tensor weight_image(const at::Tensor& input, const at::Tensor& weight, int64_t stride_h, int64_t stride_w,
+                        int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+                        int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask) {
+  TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
+  check_cuda(weight, "weight", input);
+  TORCH_CHECK(weight.dim() == 4, "weight must be 4-D");
+  c10::cuda::CUDAGuard guard(input.device());
+  dcn_conv_desc d = make_desc(input, weight.size(0), weight.size(2), weight.size(3), stride_h, stride_w, pad_h,
+                              pad_w, dilation_h, dilation_w, n_weight_grps, n_offset_grps, use_mask);
+  const size_t n = dcn_weight_image_bytes(&d);
+  auto image = at::empty({(int64_t)n}, input.options().dtype(at::kByte));
+  if (n) {
+    auto w = weight.contiguous();
+    check_status(dcn_weight_image(&d, w.data_ptr(), image.data_ptr(), n, stream_of(input)));
+  }
+  return image;
+}
+
 // Forward of the autograd path: like forward_train, and a channels_last input
 // gives a channels_last output (read and written in place by the tensor-core
 // kernels; other problems run on NCHW copies and convert the output back).
 // keep_saved: also return the state the backward reuses (else an empty tensor).
+// image: the forward weight image of `weight` (weight_image), used instead of
+// rebuilding it when non-empty and nothing is kept.
 std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_ex(
     const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
     const at::Tensor& bias, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
     int64_t dilation_h, int64_t dilation_w, int64_t n_weight_grps, int64_t n_offset_grps, bool use_mask,
-    bool keep_saved) {
+    bool keep_saved, const at::Tensor& image) {
   TORCH_CHECK(input.is_cuda(), "input must be a CUDA tensor");
   check_cuda(weight, "weight", input);
   check_cuda(offset, "offset", input);
@@ -229,7 +251,16 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_ex(
   dcn_ex_options o = ex_options(want_nhwc, want_nhwc, false);
   const bool nhwc = want_nhwc && dcn_ex_supported(&d, &o, 0);
   if (!nhwc) o = ex_options(false, false, false);
-  auto x = in_layout(input, nhwc), w = weight.contiguous(), off = offset.contiguous();
+  // an image serves every problem of this weight that takes the tensor-core
+  // forward (its size is then the weight's); others rebuild nothing and ignore it
+  const bool use_image = !keep_saved && image.defined() && image.numel() > 0 &&
+                         (size_t)image.numel() == dcn_weight_image_bytes(&d);
+  if (use_image) {
+    TORCH_CHECK(image.is_cuda() && image.device() == input.device() && image.is_contiguous(),
+                "weight image must be a contiguous tensor on the input's device");
+    o.flags = DCN_EX_WEIGHT_IMAGE;
+  }
+  auto x = in_layout(input, nhwc), w = use_image ? image : weight.contiguous(), off = offset.contiguous();
   auto m = has_mask ? mask.contiguous() : at::Tensor();
   auto b = has_bias ? bias.contiguous() : at::Tensor();
   auto out = at::empty({d.batch, d.out_channels, oh, ow},
@@ -568,6 +599,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("saved") = py::none(), py::arg("params_ready") = py::none());
   m.def("deform_conv2d_forward_ex", &deform_conv2d_forward_ex,
         "Forward of the autograd path (channels_last in, channels_last out): (output, saved)");
+  m.def("weight_image", &weight_image,
+        "Forward weight image for forward-only calls (empty when the problem is not on the tensor cores)");
   m.def("deform_conv2d_forward_train", &deform_conv2d_forward_train,
         "Forward that also returns the device state its backward reuses: (output, saved)");
   m.def("uses_tensor_cores", &uses_tensor_cores, "True when the tcgen05 kernels run this problem");

@@ -12,6 +12,7 @@ Reference: mps_deform_conv/__init__.py (v0.2.2).
 
 import math
 import threading
+import weakref
 from typing import Optional, Tuple
 
 import torch
@@ -44,6 +45,45 @@ def set_training_cache(enabled: bool) -> None:
     cost of a second bilinear gather in the weight-gradient pass."""
     global _training_cache
     _training_cache = bool(enabled)
+
+
+# Weight images of forward-only calls.  The tensor-core forward reads its
+# weights as a pre-swizzled tile image that each call otherwise rebuilds from
+# the weight.  With the cache on, a forward that keeps no state for a backward
+# reuses the image built for the same weight tensor, as long as the tensor's
+# version counter, shape, dtype, device and group split are unchanged.
+# In-place updates through the tensor (optimizer steps, ``copy_``,
+# ``load_state_dict``) bump the version counter and rebuild the image; writes
+# through ``weight.data`` bypass the counter, which is why the cache is off by
+# default.  Entries are keyed by the weight tensor's identity and dropped when
+# the tensor is freed.
+_weight_images = None
+_EMPTY = torch.empty(0, dtype=torch.uint8)  # "no image" argument of the forward
+
+
+def set_weight_image_cache(enabled: bool) -> None:
+    """Reuse (True) or rebuild per call (False, default) the forward weight image
+    of forward-only calls.  Turn it on for inference with weights that change
+    only through in-place operations on the weight tensor itself."""
+    global _weight_images
+    _weight_images = {} if enabled else None
+
+
+def _weight_image(lib, input, weight, geo):
+    """Forward weight image of `weight` (an empty tensor when the problem is
+    not on the tensor cores), from the cache when it is on and current."""
+    cache = _weight_images
+    key = (tuple(weight.shape), weight.dtype, weight.device, geo[-3])
+    if cache is not None:
+        hit = cache.get(id(weight))
+        if hit is not None and hit[0]() is weight and hit[1] == weight._version and hit[2] == key:
+            return hit[3]
+    img = lib.weight_image(input, weight, *geo)
+    if cache is not None and img.numel() > 0:
+        wid = id(weight)
+        drop = lambda _ref, c=cache, k=wid: c.pop(k, None)  # the weight was freed
+        cache[wid] = (weakref.ref(weight, drop), weight._version, key, img)
+    return img
 
 
 # ModulatedDeformConv2d reads its offset convolution's output in place (offsets
@@ -239,11 +279,15 @@ class _DeformConv2dFunction(torch.autograd.Function):
         # a channels_last input gives a channels_last output (read and written in
         # place by the tensor-core kernels)
         keep = bool(_training_cache and ctx.needs_input_grad[2])
+        image = _EMPTY
+        if not keep and _weight_images is not None:
+            image = _weight_image(lib, input, weight, (stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                                                       n_weight_grps, n_offset_grps, use_mask))
         output, saved = lib.deform_conv2d_forward_ex(
             input, weight, offset, mask_t, bias_t,
             stride_h, stride_w, pad_h, pad_w,
             dilation_h, dilation_w,
-            n_weight_grps, n_offset_grps, use_mask, keep,
+            n_weight_grps, n_offset_grps, use_mask, keep, image,
         )
         if saved.numel() == 0:
             saved = None
@@ -504,4 +548,4 @@ def is_available() -> bool:
 
 
 __all__ = ["deform_conv2d", "DeformConv2d", "ModulatedDeformConv2d", "is_available", "__version__",
-           "set_training_cache", "set_param_grad_hook", "set_head_fusion"]
+           "set_training_cache", "set_param_grad_hook", "set_head_fusion", "set_weight_image_cache"]

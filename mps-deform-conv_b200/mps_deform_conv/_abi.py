@@ -12,6 +12,9 @@ import os
 from typing import Optional
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libdcn_b200.so")
+# The same library built with -DDCN_DEBUG_BOUNDS: index checks in the gather
+# and scatter kernels (build.py builds both).
+BOUNDS_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libdcn_b200_bounds.so")
 
 DCN_FLOAT32, DCN_FLOAT16, DCN_BFLOAT16 = 0, 1, 2
 DCN_OK = 0
@@ -36,16 +39,23 @@ class DcnConvDesc(ctypes.Structure):
     ]
 
 
+class DcnBoundsRecord(ctypes.Structure):
+    """Mirror of ``dcn_bounds_record``."""
+    _fields_ = [("count", ctypes.c_uint64), ("index", ctypes.c_int64), ("extent", ctypes.c_int64),
+                ("site", ctypes.c_int32), ("width", ctypes.c_int32)]
+
+
 # name -> (restype, argtypes); the exported surface of include/dcn_b200.h
 _D = ctypes.POINTER(DcnConvDesc)
 DCN_LAYOUT_NCHW = 0
 DCN_LAYOUT_NHWC = 1
+DCN_EX_WEIGHT_IMAGE = 1
 
 
 class DcnExOptions(ctypes.Structure):
     """dcn_ex_options of include/dcn_b200.h."""
     _fields_ = [("input_layout", ctypes.c_int32), ("output_layout", ctypes.c_int32), ("head", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("flags", ctypes.c_int32)]
 
 
 _O = ctypes.POINTER(DcnExOptions)
@@ -79,6 +89,8 @@ SIGNATURES = {
                                                           _V, _SZ, _V, PARAMS_READY_FN, _V]),
     "dcn_head_supported": (ctypes.c_int, [_D]),
     "dcn_ex_supported": (ctypes.c_int, [_D, _O, ctypes.c_int]),
+    "dcn_weight_image_bytes": (_SZ, [_D]),
+    "dcn_weight_image": (ctypes.c_int, [_D, _V, _V, _SZ, _V]),
     "dcn_deform_conv2d_forward_ex": (ctypes.c_int, [_D, _O, _V, _V, _V, _V, _V, _V, _V, _SZ, _V, _SZ, _V]),
     "dcn_deform_conv2d_backward_ex": (ctypes.c_int, [_D, _O, _V, _V, _V, _V, _V, _V, _SZ, _V, _V, _V, _V, _V, _V,
                                                      _SZ, _V]),
@@ -87,22 +99,38 @@ SIGNATURES = {
                                                        _V]),
     "dcn_device_status": (ctypes.c_int, [_V]),
     "dcn_uses_tensor_cores": (ctypes.c_int, [_D]),
+    "dcn_debug_bounds_enabled": (ctypes.c_int, []),
+    "dcn_debug_bounds_read": (ctypes.c_int, [ctypes.POINTER(DcnBoundsRecord), ctypes.c_int]),
 }
 
-_lib = None
+_libs = {}
 
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Load libdcn_b200.so and declare every exported signature."""
-    global _lib
-    if _lib is None:
+    """Load libdcn_b200.so (or another build of it at `path`) once and declare
+    every exported signature."""
+    if path not in _libs:
         lib = ctypes.CDLL(path)
         for name, (res, args) in SIGNATURES.items():
             f = getattr(lib, name)
             f.restype = res
             f.argtypes = args
-        _lib = lib
-    return _lib
+        _libs[path] = lib
+    return _libs[path]
+
+
+def load_bounds() -> ctypes.CDLL:
+    """The bounds-checked build (libdcn_b200_bounds.so)."""
+    return load(BOUNDS_LIB_PATH)
+
+
+def bounds_record(lib: Optional[ctypes.CDLL] = None, reset: bool = True) -> DcnBoundsRecord:
+    """Synchronise the device and read (and by default clear) the library's
+    out-of-bounds index record; all zero unless indices left their tensors."""
+    lib = lib or load_bounds()
+    rec = DcnBoundsRecord()
+    check(lib.dcn_debug_bounds_read(ctypes.byref(rec), 1 if reset else 0), lib)
+    return rec
 
 
 class DcnError(RuntimeError):
@@ -111,9 +139,9 @@ class DcnError(RuntimeError):
         self.code = code
 
 
-def check(rc: int) -> None:
+def check(rc: int, lib: Optional[ctypes.CDLL] = None) -> None:
     if rc != DCN_OK:
-        raise DcnError(rc, load().dcn_last_error().decode())
+        raise DcnError(rc, (lib or load()).dcn_last_error().decode())
 
 
 def make_desc(dtype: int, input_shape, weight_shape, stride=(1, 1), padding=(0, 0),
@@ -156,9 +184,10 @@ def launch_count() -> int:
     return int(load().dcn_launch_count())
 
 
-def output_size(d: DcnConvDesc):
+def output_size(d: DcnConvDesc, lib: Optional[ctypes.CDLL] = None):
+    lib = lib or load()
     oh, ow = ctypes.c_int64(), ctypes.c_int64()
-    check(load().dcn_output_size(ctypes.byref(d), ctypes.byref(oh), ctypes.byref(ow)))
+    check(lib.dcn_output_size(ctypes.byref(d), ctypes.byref(oh), ctypes.byref(ow)), lib)
     return oh.value, ow.value
 
 
@@ -185,36 +214,38 @@ def desc_for(input, weight, offset, stride=(1, 1), padding=(0, 0), dilation=(1, 
 
 
 def call_forward(input, offset, weight, bias=None, stride=(1, 1), padding=(0, 0), dilation=(1, 1),
-                 mask=None):
-    """Forward through the C ABI; tensors must be contiguous CUDA tensors."""
+                 mask=None, lib: Optional[ctypes.CDLL] = None):
+    """Forward through the C ABI; tensors must be contiguous CUDA tensors.
+    `lib`: another build of the library (default libdcn_b200.so)."""
     import torch
+    lib = lib or load()
     d = desc_for(input, weight, offset, stride, padding, dilation, mask)
-    oh, ow = output_size(d)
+    oh, ow = output_size(d, lib)
     out = torch.empty((d.batch, d.out_channels, oh, ow), device=input.device, dtype=input.dtype)
-    lib = load()
     wsz = lib.dcn_forward_workspace_size(ctypes.byref(d))
     ws = torch.empty(max(wsz, 1), device=input.device, dtype=torch.uint8)
     check(lib.dcn_deform_conv2d_forward(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(offset),
                                         _ptr(mask), _ptr(bias), _ptr(out), _ptr(ws), wsz,
-                                        _stream(input)))
+                                        _stream(input)), lib)
     return out
 
 
 def call_backward(grad_output, input, offset, weight, stride=(1, 1), padding=(0, 0),
-                  dilation=(1, 1), mask=None, with_bias=True):
-    """All five gradients through the C ABI: (gI, gOff, gW, gB, gMask)."""
+                  dilation=(1, 1), mask=None, with_bias=True, lib: Optional[ctypes.CDLL] = None):
+    """All five gradients through the C ABI: (gI, gOff, gW, gB, gMask).
+    `lib`: another build of the library (default libdcn_b200.so)."""
     import torch
+    lib = lib or load()
     d = desc_for(input, weight, offset, stride, padding, dilation, mask)
     gi = torch.empty_like(input)
     goff = torch.empty_like(offset)
     gw = torch.empty_like(weight)
     gb = torch.empty(weight.shape[0], device=input.device, dtype=input.dtype) if with_bias else None
     gm = torch.empty_like(mask) if mask is not None else None
-    lib = load()
     wsz = lib.dcn_backward_workspace_size(ctypes.byref(d))
     ws = torch.empty(max(wsz, 1), device=input.device, dtype=torch.uint8)
     check(lib.dcn_deform_conv2d_backward(ctypes.byref(d), _ptr(grad_output), _ptr(input),
                                          _ptr(weight), _ptr(offset), _ptr(mask), _ptr(gi), _ptr(gw),
                                          _ptr(goff), _ptr(gm), _ptr(gb), _ptr(ws), wsz,
-                                         _stream(input)))
+                                         _stream(input)), lib)
     return gi, goff, gw, gb, gm

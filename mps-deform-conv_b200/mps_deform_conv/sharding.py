@@ -44,15 +44,16 @@ def allreduce_param_grads(grads: Sequence[Optional[torch.Tensor]], group=None,
     present = [g for g in grads if g is not None]
     if not present or not dist.is_initialized() or dist.get_world_size(group) == 1:
         return list(grads)
-    flat = torch.cat([g.reshape(-1) for g in present])
-    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
-    if average:
-        flat /= dist.get_world_size(group)
-    off = 0
-    for g in present:
-        n = g.numel()
-        g.copy_(flat[off:off + n].view_as(g))
-        off += n
+    with torch.cuda.nvtx.range("dcn_param_allreduce"):
+        flat = torch.cat([g.reshape(-1) for g in present])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        if average:
+            flat /= dist.get_world_size(group)
+        off = 0
+        for g in present:
+            n = g.numel()
+            g.copy_(flat[off:off + n].view_as(g))
+            off += n
     return list(grads)
 
 

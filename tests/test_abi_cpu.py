@@ -27,6 +27,18 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert set(_abi.SIGNATURES) == set(names)
 
 
+def test_bounds_library_exports_the_same_surface():
+    """libdcn_b200_bounds.so (build.py, -DDCN_DEBUG_BOUNDS) exports the same
+    symbols; only it reports the index checks as compiled in."""
+    from mps_deform_conv import _abi
+    assert os.path.exists(_abi.BOUNDS_LIB_PATH)
+    blib = _abi.load_bounds()
+    for n in declared_functions():
+        assert hasattr(blib, n), f"libdcn_b200_bounds.so does not export {n}"
+    assert blib.dcn_debug_bounds_enabled() == 1
+    assert _abi.load().dcn_debug_bounds_enabled() == 0
+
+
 def test_abi_version():
     from mps_deform_conv import _abi
     assert _abi.load().dcn_abi_version() >= 100
@@ -167,6 +179,37 @@ def test_ex_layout_options_checked_without_launching():
     rc = lib.dcn_deform_conv2d_forward_ex(ctypes.byref(tc), None, None, None, None, None, None, None, None, 0,
                                           None, 0, None)
     assert rc == _abi.DCN_ERR_INVALID_ARGUMENT and "NULL" in lib.dcn_last_error().decode()
+
+
+def test_weight_image_queries_and_flag_checks():
+    """Forward weight images: the size query, and the options that accept or
+    reject DCN_EX_WEIGHT_IMAGE (host logic, nothing launches)."""
+    from mps_deform_conv import _abi
+    lib = _abi.load()
+    tc = _desc(dtype=_abi.DCN_BFLOAT16, input_shape=(2, 128, 16, 16), weight_shape=(64, 64, 3, 3),
+               padding=(1, 1), use_mask=True, n_weight_grps=2)
+    f32 = _desc(input_shape=(2, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1), use_mask=True)
+    assert lib.dcn_weight_image_bytes(ctypes.byref(tc)) == 64 * 64 * 9 * 2
+    assert lib.dcn_weight_image_bytes(ctypes.byref(f32)) == 0
+    img = _abi.DcnExOptions(_abi.DCN_LAYOUT_NCHW, _abi.DCN_LAYOUT_NCHW, 0, _abi.DCN_EX_WEIGHT_IMAGE)
+    img_nhwc = _abi.DcnExOptions(_abi.DCN_LAYOUT_NHWC, _abi.DCN_LAYOUT_NHWC, 0, _abi.DCN_EX_WEIGHT_IMAGE)
+    unknown = _abi.DcnExOptions(_abi.DCN_LAYOUT_NCHW, _abi.DCN_LAYOUT_NCHW, 0, 2)
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(img), 0) == 1
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(img_nhwc), 0) == 1
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(img), 1) == 0      # forward only
+    assert lib.dcn_ex_supported(ctypes.byref(f32), ctypes.byref(img), 0) == 0     # tensor-core problems only
+    assert lib.dcn_ex_supported(ctypes.byref(tc), ctypes.byref(unknown), 0) == 0  # unknown flag bits
+    p = ctypes.c_void_p(16)
+    rc = lib.dcn_weight_image(ctypes.byref(f32), p, p, 1 << 20, None)
+    assert rc == _abi.DCN_ERR_UNSUPPORTED
+    rc = lib.dcn_weight_image(ctypes.byref(tc), p, p, 100, None)
+    assert rc == _abi.DCN_ERR_WORKSPACE
+    rc = lib.dcn_weight_image(ctypes.byref(tc), p, ctypes.c_void_p(24), 1 << 20, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT and "16-byte" in lib.dcn_last_error().decode()
+    # an image with saved state is refused before anything launches
+    rc = lib.dcn_deform_conv2d_forward_ex(ctypes.byref(tc), ctypes.byref(img), p, p, p, p, None, p, p, 1 << 40,
+                                          p, 1 << 40, None)
+    assert rc == _abi.DCN_ERR_INVALID_ARGUMENT and "forward-only" in lib.dcn_last_error().decode()
 
 
 @pytest.mark.parametrize("kw,expect", [
