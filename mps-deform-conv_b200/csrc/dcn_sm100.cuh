@@ -154,6 +154,27 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool ab_bf16) {
          | ((uint32_t)(M >> 4) << 24);              // M / 16
 }
 
+// Instruction descriptor of kind::tf32 (format code 2 for A and B) with fp32
+// accumulation, both operands K-major.  One instruction is M x N x 8.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4)                                  // D format: f32
+         | (2u << 7)                                // A format: tf32
+         | (2u << 10)                               // B format: tf32
+         | ((uint32_t)(N >> 3) << 17)               // N / 8
+         | ((uint32_t)(M >> 4) << 24);              // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T on tf32 operands (M x N x 8), one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, one instruction (M x N x 16), issued by
 // one thread.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,

@@ -773,8 +773,9 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         if (lane == 0) mbar_arrive(d_empty(e));  // TMEM buffer read completely
       }
       __syncwarp();
-      // ---- phase 2: lane = (pixel, offset group), 4 pixels per step; the
-      // offsets and mask of step it+1 are loaded during step it
+      // ---- phase 2: lane = (pixel, offset group), 4 pixels per step.  The
+      // record of step it+1 is in flight while step it is processed, and the
+      // offsets and mask of step it+2 while step it+1's record is requested.
       auto load_sample = [&](int row, T& dy, T& dx, T& mr) {
         const int4 p4 = ws->pix[row];
         if (p4.x >= 0) {
@@ -787,14 +788,36 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
                           : from_f<T>(1.f);
         }
       };
-      T ndy = from_f<T>(0.f), ndx = from_f<T>(0.f), nmr = from_f<T>(1.f);
-      load_sample(rsub, ndy, ndx, nmr);
+      // the sample's corner-quad record (two 256-bit loads) when its floor
+      // lies in [-1, H-1] x [-1, W-1] (other samples have no corner in the
+      // image); returns the record index, or -1 with zeros
+      auto fetch = [&](int row, T dy, T dx, uint4 (&xv)[4]) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xv[k] = make_uint4(0, 0, 0, 0);
+        const int4 p4 = ws->pix[row];
+        if (p4.x < 0) return -1;
+        const SamplePos sp = sample_pos(p4.z + kw.ti * g.dh, p4.w + kw.tj * g.dw, to_f(dy), to_f(dx));
+        if (!(sp.y0 >= -1 && sp.y0 < g.H && sp.x0 >= -1 && sp.x0 < g.W)) return -1;
+        const int rec = ((p4.x * (g.H + 1) + sp.y0 + 1) * W1 + sp.x0 + 1) * OG + o;
+        const T* r = xq + DCN_BOUND((uint32_t)rec * 32u, 32, quad_elems(g), DBG_TC_GATHER_QUAD);
+        ldg256(r, xv[0], xv[1]);
+        ldg256(r + 16, xv[2], xv[3]);
+        return rec;
+      };
+      T cdy = from_f<T>(0.f), cdx = from_f<T>(0.f), cmr = from_f<T>(1.f);  // step it
+      T ndy = from_f<T>(0.f), ndx = from_f<T>(0.f), nmr = from_f<T>(1.f);  // step it+1
+      load_sample(rsub, cdy, cdx, cmr);
+      load_sample(rsub + 4, ndy, ndx, nmr);
+      uint4 xc[4], xn[4];
+      int crec = fetch(rsub, cdy, cdx, xc);
 #pragma unroll 1
       for (int it = 0; it < 8; ++it) {
         const int rr = it * 4 + rsub;
+        int nrec = -1;
+        T n2dy = from_f<T>(0.f), n2dx = from_f<T>(0.f), n2mr = from_f<T>(1.f);
+        if (it + 1 < 8) nrec = fetch(rr + 4, ndy, ndx, xn);
+        if (it + 2 < 8) load_sample(rr + 8, n2dy, n2dx, n2mr);
         const int4 px = ws->pix[rr];
-        const T cdy = ndy, cdx = ndx, cmr = nmr;
-        if (it + 1 < 8) load_sample(rr + 4, ndy, ndx, nmr);
         const uint4 gd = *reinterpret_cast<const uint4*>(ws->slab[rr] + ((j8 ^ (rr & 7)) << 2));
         float gc[8];
         {
@@ -808,25 +831,15 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         if (px.x >= 0) {
           const long long ob = DCN_BOUND((long long)px.x * g.off_bs + (long long)(o * 2 * g.T + 2 * kw.t) * g.HWo + px.y,
                                          g.HWo + 1, g.B * g.off_bs, DBG_DG_COORD);
-          const float dy = to_f(cdy), dx = to_f(cdx);
           const float m = g.use_mask ? mask_of(g, to_f(cmr)) : 1.f;
-          const SamplePos sp = sample_pos(px.z + kw.ti * g.dh, px.w + kw.tj * g.dw, dy, dx);
+          const SamplePos sp = sample_pos(px.z + kw.ti * g.dh, px.w + kw.tj * g.dw, to_f(cdy), to_f(cdx));
           const Corners cs = corners_of(sp, g.H, g.W);
-          // the record covers every corner of a sample whose floor lies in
-          // [-1, H-1] x [-1, W-1]; other samples have no corner in the image
-          uint4 xv[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                         make_uint4(0, 0, 0, 0)};
-          if (sp.y0 >= -1 && sp.y0 < g.H && sp.x0 >= -1 && sp.x0 < g.W) {
-            rec = ((px.x * (g.H + 1) + sp.y0 + 1) * W1 + sp.x0 + 1) * OG + o;
-            const T* r = xq + DCN_BOUND((uint32_t)rec * 32u, 32, quad_elems(g), DBG_TC_GATHER_QUAD);
-            ldg256(r, xv[0], xv[1]);
-            ldg256(r + 16, xv[2], xv[3]);
-          }
+          rec = crec;
           float d[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const float2 x01 = Vec<T>::unpack(xv[k].x), x23 = Vec<T>::unpack(xv[k].y),
-                         x45 = Vec<T>::unpack(xv[k].z), x67 = Vec<T>::unpack(xv[k].w);
+            const float2 x01 = Vec<T>::unpack(xc[k].x), x23 = Vec<T>::unpack(xc[k].y),
+                         x45 = Vec<T>::unpack(xc[k].z), x67 = Vec<T>::unpack(xc[k].w);
             d[k] = gc[0] * x01.x + gc[1] * x01.y + gc[2] * x23.x + gc[3] * x23.y + gc[4] * x45.x + gc[5] * x45.y +
                    gc[6] * x67.x + gc[7] * x67.y;
           }
@@ -876,6 +889,12 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           }
           __syncwarp();  // the staging area is rewritten by the next step
         }
+        // rotate: step it+1 becomes current
+        cdy = ndy; cdx = ndx; cmr = nmr;
+        ndy = n2dy; ndx = n2dx; nmr = n2mr;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xc[k] = xn[k];
+        crec = nrec;
       }
       __syncwarp();  // the next chunk's phase 1 rewrites the slab
     }

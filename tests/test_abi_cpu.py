@@ -98,15 +98,17 @@ def test_workspace_sizes_are_host_queries():
                        "dcn_backward_input_workspace_size", "dcn_saved_state_bytes"):
                 assert getattr(lib, fn)(ctypes.byref(q)) >= 0
             assert lib.dcn_head_supported(ctypes.byref(q)) in (0, 1)
-    # an fp32 problem whose output tiles fill less than a wave splits K in the
-    # forward (9 partials here); with at least a wave of (pixel, tap, offset
-    # group) threads the forward also materializes fp32 columns [C*T][P]
+    # the fp32 forward materializes its columns [C*T][P] (fp32) for the
+    # tensor-core GEMM, in slices of whole images of at most 1 GiB
     small = _desc(input_shape=(1, 64, 16, 16), weight_shape=(64, 64, 3, 3), padding=(1, 1))
-    assert lib.dcn_forward_workspace_size(ctypes.byref(small)) == 9 * 64 * 256 * 4
-    # 2x128x64x64: fp32 columns [C*T][P], and K split 3 ways so that its 64
-    # tiles of 128 x 128 make a wave (3 fp32 partial outputs [Co][P])
+    assert lib.dcn_forward_workspace_size(ctypes.byref(small)) == 64 * 9 * 256 * 4
+    big = _desc(input_shape=(4, 64, 512, 512), weight_shape=(64, 64, 3, 3), padding=(1, 1))
+    per_image = 64 * 9 * 512 * 512 * 4  # 604 MB: one image per slice
+    assert lib.dcn_forward_workspace_size(ctypes.byref(big)) == per_image
+    # 2x128x64x64: both images in one slice; the GEMM writes the output
+    # directly (no K-split partials)
     c2 = _desc(input_shape=(2, 128, 64, 64), weight_shape=(128, 128, 3, 3), padding=(1, 1), use_mask=True)
-    assert lib.dcn_forward_workspace_size(ctypes.byref(c2)) == 128 * 9 * 8192 * 4 + 3 * 128 * 8192 * 4
+    assert lib.dcn_forward_workspace_size(ctypes.byref(c2)) == 128 * 9 * 8192 * 4
 
 
 def test_forward_rejects_null_and_small_workspace_without_launching():

@@ -131,12 +131,16 @@ def test_empty_batch(cuda):
     assert torch.count_nonzero(w.grad) == 0 and torch.count_nonzero(b.grad) == 0
 
 
-@pytest.mark.parametrize("shape", [(1, 64, 16, 16, 64, 1), (2, 32, 12, 10, 48, 2)])
-def test_simt_forward_k_split_vs_oracle(shape, cuda):
-    """fp32 problems whose output tiles fill less than one wave split the
-    reduction over K; the splits are added in a fixed order, so the forward
-    stays deterministic and matches the oracle."""
+@pytest.mark.parametrize("shape", [(1, 64, 16, 16, 64, 1), (2, 32, 12, 10, 48, 2), (3, 40, 9, 11, 200, 1)])
+def test_fp32_tensor_core_gemms_vs_oracle(shape, cuda):
+    """fp32 problems materialize their columns and run the three GEMMs on the
+    tensor cores (tf32 MMAs with the hi/lo split): forward bitwise repeatable,
+    forward and all five gradients at fp32 tolerance against the oracle.
+    The shapes cover row/column tile tails (200 output channels = a 128 and a
+    72-wide tile; K = 40*9 = 360, not a multiple of the 32-deep K chunk) and
+    groups."""
     from mps_deform_conv import _abi
+    import mps_deform_conv as mdc
     B, C, H, W, Co, G = shape
     g = torch.Generator().manual_seed(53)
     x = torch.randn(B, C, H, W, generator=g)
@@ -144,16 +148,25 @@ def test_simt_forward_k_split_vs_oracle(shape, cuda):
     off = torch.randn(B, 18, H, W, generator=g) * 1.5
     m = torch.sigmoid(torch.randn(B, 9, H, W, generator=g))
     b = torch.randn(Co, generator=g) * 0.1
+    go = torch.randn(B, Co, H, W, generator=g)
     d = _abi.desc_for(x, w, off, (1, 1), (1, 1), (1, 1), m)
     lib = _abi.load()
-    assert lib.dcn_forward_workspace_size(ctypes.byref(d)) > 0  # the split partial sums
+    assert lib.dcn_forward_workspace_size(ctypes.byref(d)) == (4 * C * 9 * B * H * W + 255) // 256 * 256  # fp32 columns
     dev = [t.to(cuda) for t in (x, off, w, b, m)]
     a = _abi.call_forward(dev[0], dev[1], dev[2], dev[3], (1, 1), (1, 1), (1, 1), dev[4])
     a2 = _abi.call_forward(dev[0], dev[1], dev[2], dev[3], (1, 1), (1, 1), (1, 1), dev[4])
     torch.cuda.synchronize()
     assert torch.equal(a, a2)
     ref = oracle.forward(x, off, w, b, (1, 1), (1, 1), (1, 1), m)
-    assert_close(a, ref, "float32", 'a')
+    assert_close(a, ref, "float32", "output")
+    leaves = [t.clone().requires_grad_(True) for t in dev]
+    out = mdc.deform_conv2d(leaves[0], leaves[1], leaves[2], leaves[3], 1, 1, 1, leaves[4])
+    grads = torch.autograd.grad(out, leaves, go.to(cuda))
+    refs = oracle.backward(go.double(), x.double(), off.double(), w.double(), (1, 1), (1, 1), (1, 1),
+                           m.double(), True)
+    for nm, gv, rv in zip(("grad_input", "grad_offset", "grad_weight", "grad_bias", "grad_mask"),
+                          (grads[0], grads[1], grads[2], grads[3], grads[4]), refs):
+        assert_close(gv, rv, "float32", nm)
 
 
 def test_device_status_clean_after_runs(cuda):
