@@ -47,28 +47,50 @@ static cudaError_t launch_gemm(const char* name, const LA& la, const LB& lb, con
 }
 
 // ---------------------------------------------------------------- functors
+// Operand loaders: float operator()(g, k, mn) reads one element.  kContig
+// says which 4 consecutive elements are contiguous in memory (1: k..k+3 at
+// one mn, 2: mn..mn+3 at one k, 0: neither); when `vec` is set (fp32 data,
+// 16-byte aligned rows, set by the host) ld4(g, k, mn) reads them as one
+// float4 at a k (kContig 1) or mn (kContig 2) that is a multiple of 4.
+__host__ __device__ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
 template <typename T>
 struct WeightRowLoader {  // A(k, m) = W[g*Cog + m][k]   (forward)
-  const T* w; int Cog, Kg;
+  static constexpr int kContig = 1;
+  const T* w; int Cog, Kg; bool vec;
+  WeightRowLoader(const T* w_, int cog, int kg)
+      : w(w_), Cog(cog), Kg(kg), vec(sizeof(T) == 4 && kg % 4 == 0 && aligned16(w_)) {}
   __device__ float operator()(int g, int k, int m) const {
     return to_f(w[(long long)(g * Cog + m) * Kg + k]);
+  }
+  __device__ float4 ld4(int g, int k, int m) const {
+    return *reinterpret_cast<const float4*>(w + (long long)(g * Cog + m) * Kg + k);
   }
 };
 template <typename T>
 struct WeightColLoader {  // A(co, m=k) = W[g*Cog + co][k]   (dgrad)
-  const T* w; int Cog, Kg;
+  static constexpr int kContig = 2;
+  const T* w; int Cog, Kg; bool vec;
+  WeightColLoader(const T* w_, int cog, int kg)
+      : w(w_), Cog(cog), Kg(kg), vec(sizeof(T) == 4 && kg % 4 == 0 && aligned16(w_)) {}
   __device__ float operator()(int g, int co, int k) const {
     return to_f(w[(long long)(g * Cog + co) * Kg + k]);
+  }
+  __device__ float4 ld4(int g, int co, int k) const {
+    return *reinterpret_cast<const float4*>(w + (long long)(g * Cog + co) * Kg + k);
   }
 };
 template <typename T>
 struct ColumnLoader {  // B(k, n) = col[(g*Cig + k/T)*T + k%T][n]   (forward)
-  Geom geo; const T* x; const T* off; const T* msk;
+  static constexpr int kContig = 0;
+  Geom geo; const T* x; const T* off; const T* msk; bool vec = false;
+  ColumnLoader(const Geom& g_, const T* x_, const T* off_, const T* msk_) : geo(g_), x(x_), off(off_), msk(msk_) {}
   __device__ float operator()(int g, int k, int n) const {
     const int b = n / geo.HWo, p = n - b * geo.HWo;
     const int cl = k / geo.T, t = k - cl * geo.T;
     return column_value(geo, x, off, msk, b, g * geo.Cig + cl, t, p);
   }
+  __device__ float4 ld4(int, int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
 };
 // n / d for 0 <= n: a float-reciprocal quotient corrected to the exact one
 // (n < 2^24), else the integer division.
@@ -80,29 +102,55 @@ __device__ __forceinline__ int div_rcp(int n, int d, float rcp) {
   else if (r >= d) ++q;
   return q;
 }
+// grad_output rows: 4 consecutive pixels px..px+3 (px a multiple of 4) are one
+// image's when HWo is a multiple of 4.
 template <typename T>
 struct GradOutLoaderCN {  // B(co, n=px) = gO[b][g*Cog + co][p]   (dgrad)
-  Geom geo; const T* go; float rcp_hwo;
+  static constexpr int kContig = 2;
+  Geom geo; const T* go; float rcp_hwo; bool vec;
+  GradOutLoaderCN(const Geom& g_, const T* go_)
+      : geo(g_), go(go_), rcp_hwo(1.f / (float)g_.HWo), vec(sizeof(T) == 4 && g_.HWo % 4 == 0 && aligned16(go_)) {}
   __device__ float operator()(int g, int co, int n) const {
     const int b = div_rcp(n, geo.HWo, rcp_hwo), p = n - b * geo.HWo;
     return to_f(go[((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p]);
   }
+  __device__ float4 ld4(int g, int co, int n) const {
+    const int b = div_rcp(n, geo.HWo, rcp_hwo), p = n - b * geo.HWo;
+    return *reinterpret_cast<const float4*>(go + ((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p);
+  }
 };
 template <typename T>
 struct GradOutLoaderPM {  // A(px, m=co) = gO[b][g*Cog + co][p]   (wgrad)
-  Geom geo; const T* go; float rcp_hwo;
+  static constexpr int kContig = 1;
+  Geom geo; const T* go; float rcp_hwo; bool vec;
+  GradOutLoaderPM(const Geom& g_, const T* go_)
+      : geo(g_), go(go_), rcp_hwo(1.f / (float)g_.HWo), vec(sizeof(T) == 4 && g_.HWo % 4 == 0 && aligned16(go_)) {}
   __device__ float operator()(int g, int px, int co) const {
     const int b = div_rcp(px, geo.HWo, rcp_hwo), p = px - b * geo.HWo;
     return to_f(go[((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p]);
   }
+  __device__ float4 ld4(int g, int px, int co) const {
+    const int b = div_rcp(px, geo.HWo, rcp_hwo), p = px - b * geo.HWo;
+    return *reinterpret_cast<const float4*>(go + ((long long)b * geo.Co + g * geo.Cog + co) * geo.HWo + p);
+  }
 };
 struct ColumnBufferLoader {  // B(k, n) = cols[(g*Kg + k)][n]   (forward, materialized columns)
-  const float* cols; int Kg; long long P;
+  static constexpr int kContig = 2;
+  const float* cols; int Kg; long long P; bool vec;
+  ColumnBufferLoader(const float* c, int kg, long long p) : cols(c), Kg(kg), P(p), vec(p % 4 == 0 && aligned16(c)) {}
   __device__ float operator()(int g, int k, int n) const { return cols[((long long)g * Kg + k) * P + n]; }
+  __device__ float4 ld4(int g, int k, int n) const {
+    return *reinterpret_cast<const float4*>(cols + ((long long)g * Kg + k) * P + n);
+  }
 };
 struct ColumnBufferLoaderPK {  // B(px, n=k) = cols[(g*Kg + k)][px]   (wgrad, materialized columns)
-  const float* cols; int Kg; long long P;
+  static constexpr int kContig = 1;
+  const float* cols; int Kg; long long P; bool vec;
+  ColumnBufferLoaderPK(const float* c, int kg, long long p) : cols(c), Kg(kg), P(p), vec(p % 4 == 0 && aligned16(c)) {}
   __device__ float operator()(int g, int px, int k) const { return cols[((long long)g * Kg + k) * P + px]; }
+  __device__ float4 ld4(int g, int px, int k) const {
+    return *reinterpret_cast<const float4*>(cols + ((long long)g * Kg + k) * P + px);
+  }
 };
 template <typename T>
 struct ForwardEpilogue {  // out[b][g*Cog + m][p] = acc + bias
@@ -388,9 +436,9 @@ template <typename T>
 cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
                          const T* bias, T* out, void* workspace, cudaStream_t st) {
   const int Kg = g.Cig * g.T;
-  WeightRowLoader<T> la{w, g.Cog, Kg};
+  WeightRowLoader<T> la(w, g.Cog, Kg);
   if (!workspace || simt_fwd_cols_bytes(g) == 0) {  // no column buffer: the loader gathers
-    ColumnLoader<T> lb{g, x, off, msk};
+    ColumnLoader<T> lb(g, x, off, msk);
     return launch_gemm<true, false>("tf32_fwd_gemm", la, lb, ForwardEpilogue<T>{g, bias, out}, g.Cog, (int)g.P,
                                     Kg, g.G, false, st);
   }
@@ -411,7 +459,7 @@ cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, co
       im2col_og_kernel<T, float><<<grid_for(im2col_threads(gs)), 256, 0, st>>>(gs, xs, offs, msks, cols);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    ColumnBufferLoader lb{cols, Kg, gs.P};
+    ColumnBufferLoader lb(cols, Kg, gs.P);
     if ((e = launch_gemm<true, false>("tf32_fwd_gemm", la, lb, ForwardEpilogue<T>{gs, bias, outs}, gs.Cog,
                                       (int)gs.P, Kg, gs.G, false, st)) != cudaSuccess)
       return e;
@@ -477,7 +525,7 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
   if (gw) {
     float* gw32 = ws.gw32 ? ws.gw32 : reinterpret_cast<float*>(gw);
     if ((e = cudaMemsetAsync(gw32, 0, sizeof(float) * (size_t)g.Co * Kg, st)) != cudaSuccess) return e;
-    GradOutLoaderPM<T> la{g, go, 1.f / (float)g.HWo};
+    GradOutLoaderPM<T> la(g, go);
     AtomicWeightEpilogue ep{gw32, g.Cog, Kg};
     // the columns, one sample per (pixel, tap, offset group), in the column
     // gradient's buffer (free until the dgrad GEMM below writes it)
@@ -486,15 +534,15 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
       im2col_og_kernel<T, float><<<grid_for(im2col_threads(g)), 256, 0, st>>>(g, x, off, msk, ws.gcol);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    ColumnBufferLoaderPK lb{ws.gcol, Kg, g.P};
+    ColumnBufferLoaderPK lb(ws.gcol, Kg, g.P);
     if ((e = launch_gemm<true, true>("tf32_wgrad_gemm", la, lb, ep, g.Cog, Kg, (int)g.P, g.G, true, st)) !=
         cudaSuccess)
       return e;
     if (ws.gw32 && (e = convert_f32<T>(ws.gw32, gw, (long long)g.Co * Kg, st)) != cudaSuccess) return e;
   }
   if (gin || goff || gmsk) {
-    WeightColLoader<T> la{w, g.Cog, Kg};
-    GradOutLoaderCN<T> lb{g, go, 1.f / (float)g.HWo};
+    WeightColLoader<T> la(w, g.Cog, Kg);
+    GradOutLoaderCN<T> lb(g, go);
     ColumnStoreEpilogue ep{ws.gcol, Kg, g.P};
     if ((e = launch_gemm<false, false>("tf32_dgrad_gemm", la, lb, ep, Kg, (int)g.P, g.Cog, g.G, false, st)) !=
         cudaSuccess)

@@ -68,53 +68,105 @@ __device__ __forceinline__ uint32_t to_tf32(float x) {
   return r;
 }
 
-// Rows [0, ROWS) x K values [k0, k0 + 32) of one operand: ROWS * 8 items
-// (row, 4-value chunk) over the NPROD producer threads, ITEMS per thread.
-// KFAST: the source is contiguous along K, 8 consecutive threads read one
-// row's 32 values; else contiguous along the rows, consecutive threads read
-// consecutive rows.  Either way a warp's 16-byte shared stores of one phase
-// hit 8 distinct chunk positions.
-template <int ROWS, bool KFAST>
-struct TileMap {
-  static constexpr int ITEMS = ROWS * 8 / NPROD;
-  static_assert(ITEMS >= 1 && ROWS * 8 % NPROD == 0, "tile rows");
-  __device__ __forceinline__ static int row(int it) { return KFAST ? it >> 3 : it % ROWS; }
-  __device__ __forceinline__ static int chunk(int it) { return KFAST ? it & 7 : it / ROWS; }
-};
-
+// Rows [0, ROWS) x K values [k0, k0 + 32) of one operand, loaded into
+// registers (load) and then written as hi = tf32(x), lo = tf32(x - hi) into
+// the tile pair (store).  The items a thread owns depend on the loader's
+// contiguity (L::kContig):
+//   2 (rows contiguous): item = (4-row group, 4-value K chunk): four float4
+//     reads (one per k) of 4 consecutive rows, written as 4 row chunks;
+//     consecutive threads take consecutive row groups (coalesced);
+//   1 (K contiguous): item = (row, chunk), one float4 read; 8 consecutive
+//     threads read one row's 32 values;
+//   0: item = (row, chunk), four element reads; KFAST picks the thread order
+//     (8 threads per row, or consecutive rows).
+// Reads fall back to elements at the tile's edges or when L::vec is unset.
 template <int ROWS, bool KFAST, class L>
-__device__ __forceinline__ void load_vals(const L& ld, int g, int k0, int kend, int mn0, int mnend, int tid,
-                                          float (&v)[TileMap<ROWS, KFAST>::ITEMS][4]) {
-  using TM = TileMap<ROWS, KFAST>;
-#pragma unroll
-  for (int i = 0; i < TM::ITEMS; ++i) {
-    const int it = tid + i * NPROD;
-    const int mn = mn0 + TM::row(it), kq = k0 + 4 * TM::chunk(it);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[i][e] = (kq + e < kend && mn < mnend) ? ld(g, kq + e, mn) : 0.0f;
-  }
-}
+struct Fill {
+  static constexpr int C = L::kContig;
+  static constexpr int NITEMS = C == 2 ? ROWS * 2 : ROWS * 8;
+  static constexpr int NI = (NITEMS + NPROD - 1) / NPROD;
+  static constexpr int NV = C == 2 ? 16 : 4;
+  static_assert(ROWS % 32 == 0 && (NITEMS % NPROD == 0 || NITEMS < NPROD), "tile rows");
+  float v[NI][NV];
 
-// The values as hi = tf32(x) and lo = tf32(x - hi) into the tile pair.
-template <int ROWS, bool KFAST>
-__device__ __forceinline__ void store_split(const float (&v)[TileMap<ROWS, KFAST>::ITEMS][4], uint8_t* hi,
-                                            uint8_t* lo, int tid) {
-  using TM = TileMap<ROWS, KFAST>;
+  __device__ __forceinline__ static void item(int it, int& r, int& j) {
+    if (C == 2) { r = 4 * (it % (ROWS / 4)); j = it / (ROWS / 4); }
+    else if (C == 1 || KFAST) { r = it >> 3; j = it & 7; }
+    else { r = it % ROWS; j = it / ROWS; }
+  }
+
+  __device__ __forceinline__ void load(const L& ld, int g, int k0, int kend, int mn0, int mnend, int tid) {
 #pragma unroll
-  for (int i = 0; i < TM::ITEMS; ++i) {
-    const int it = tid + i * NPROD;
-    const int r = TM::row(it), j = TM::chunk(it);
+    for (int i = 0; i < NI; ++i) {
+      const int it = tid + i * NPROD;
+      if (it >= NITEMS) break;
+      int r, j;
+      item(it, r, j);
+      const int mn = mn0 + r, kq = k0 + 4 * j;
+      if (C == 2) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = kq + e;
+          if (ld.vec && k < kend && mn + 3 < mnend) {
+            const float4 f = ld.ld4(g, k, mn);
+            v[i][4 * e] = f.x; v[i][4 * e + 1] = f.y; v[i][4 * e + 2] = f.z; v[i][4 * e + 3] = f.w;
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[i][4 * e + q] = (k < kend && mn + q < mnend) ? ld(g, k, mn + q) : 0.0f;
+          }
+        }
+      } else if (C == 1 && ld.vec && kq + 3 < kend && mn < mnend) {
+        const float4 f = ld.ld4(g, kq, mn);
+        v[i][0] = f.x; v[i][1] = f.y; v[i][2] = f.z; v[i][3] = f.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[i][e] = (kq + e < kend && mn < mnend) ? ld(g, kq + e, mn) : 0.0f;
+      }
+    }
+  }
+
+  __device__ __forceinline__ static void put(uint8_t* hi, uint8_t* lo, int r, int j, float a, float b, float c,
+                                             float d) {
+    const float x[4] = {a, b, c, d};
     uint32_t h[4], l[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      h[e] = to_tf32(v[i][e]);
-      l[e] = to_tf32(v[i][e] - __uint_as_float(h[e]));
+      h[e] = to_tf32(x[e]);
+      l[e] = to_tf32(x[e] - __uint_as_float(h[e]));
     }
     const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4);
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
-}
+
+  __device__ __forceinline__ void store(uint8_t* hi, uint8_t* lo, int tid) const {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int it = tid + i * NPROD;
+      if (it >= NITEMS) break;
+      int r, j;
+      item(it, r, j);
+      if (C == 2) {
+        // the 4 rows in an order rotated by rot = (r / 8) % 4, so that the 8
+        // lanes of a store phase write rows of 8 distinct (row % 8), i.e.
+        // 8 distinct chunk positions (no bank conflicts)
+        const int rot = (r >> 3) & 3;
+        float a[4][4];  // a[e][q] = v[4e + (q + rot) % 4]
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float a0 = v[i][4 * e], a1 = v[i][4 * e + 1], a2 = v[i][4 * e + 2], a3 = v[i][4 * e + 3];
+          if (rot & 1) { const float t = a0; a0 = a1; a1 = a2; a2 = a3; a3 = t; }
+          if (rot & 2) { float t = a0; a0 = a2; a2 = t; t = a1; a1 = a3; a3 = t; }
+          a[e][0] = a0; a[e][1] = a1; a[e][2] = a2; a[e][3] = a3;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) put(hi, lo, r + ((q + rot) & 3), j, a[0][q], a[1][q], a[2][q], a[3][q]);
+      } else {
+        put(hi, lo, r, j, v[i][0], v[i][1], v[i][2], v[i][3]);
+      }
+    }
+  }
+};
 
 // grid (ceil(Ccols / BN), ceil(Rrows / BM), groups * splits); blockIdx.z =
 // group * splits + split, the split owning K range [split*kps, +kps).
@@ -168,38 +220,38 @@ tf32x3_gemm_kernel(const LR lr, const LC lc, const EP ep, int Rrows, int Ccols, 
     // ------------------------------------------------ operand producers
     // chunks i+1 and i+2 have their loads in flight while chunk i is split
     // and stored (three register sets, used in rotation)
-    using TR = TileMap<BM, R_KFAST>;
-    using TC = TileMap<BN, C_KFAST>;
+    using FR = Fill<BM, R_KFAST, LR>;
+    using FC = Fill<BN, C_KFAST, LC>;
     const int tid = threadIdx.x;
-    float rv0[TR::ITEMS][4], cv0[TC::ITEMS][4], rv1[TR::ITEMS][4], cv1[TC::ITEMS][4];
-    float rv2[TR::ITEMS][4], cv2[TC::ITEMS][4];
-    auto load = [&](int i, float (&rv)[TR::ITEMS][4], float (&cv)[TC::ITEMS][4]) {
+    FR fr0, fr1, fr2;
+    FC fc0, fc1, fc2;
+    auto load = [&](int i, FR& fr, FC& fc) {
       if (i >= nk) return;
       const int k0 = kbeg + i * BKF;
-      load_vals<BM, R_KFAST>(lr, g, k0, kend, r0, Rrows, tid, rv);
-      load_vals<BN, C_KFAST>(lc, g, k0, kend, c0, Ccols, tid, cv);
+      fr.load(lr, g, k0, kend, r0, Rrows, tid);
+      fc.load(lc, g, k0, kend, c0, Ccols, tid);
     };
-    auto store = [&](int i, const float (&rv)[TR::ITEMS][4], const float (&cv)[TC::ITEMS][4]) {
+    auto store = [&](int i, const FR& fr, const FC& fc) {
       const int s = i % STAGES;
       if (!mbar_wait(empty(s), ((i / STAGES) & 1) ^ 1, abort_flag, status, ST_G_PROD)) return false;
       uint8_t* rt = smem + L.r + (uint32_t)s * 2 * R_TILE;
       uint8_t* ct = smem + L.c + (uint32_t)s * 2 * C_TILE;
-      store_split<BM, R_KFAST>(rv, rt, rt + R_TILE, tid);
-      store_split<BN, C_KFAST>(cv, ct, ct + C_TILE, tid);
+      fr.store(rt, rt + R_TILE, tid);
+      fc.store(ct, ct + C_TILE, tid);
       fence_async_shared();
       mbar_arrive(full(s));
       return true;
     };
     bool ok = true;
-    load(0, rv0, cv0);
-    load(1, rv1, cv1);
+    load(0, fr0, fc0);
+    load(1, fr1, fc1);
     for (int i = 0; i < nk; i += 3) {
-      load(i + 2, rv2, cv2);
-      if (!(ok = store(i, rv0, cv0)) || i + 1 >= nk) break;
-      load(i + 3, rv0, cv0);
-      if (!(ok = store(i + 1, rv1, cv1)) || i + 2 >= nk) break;
-      load(i + 4, rv1, cv1);
-      if (!(ok = store(i + 2, rv2, cv2))) break;
+      load(i + 2, fr2, fc2);
+      if (!(ok = store(i, fr0, fc0)) || i + 1 >= nk) break;
+      load(i + 3, fr0, fc0);
+      if (!(ok = store(i + 1, fr1, fc1)) || i + 2 >= nk) break;
+      load(i + 4, fr1, fc1);
+      if (!(ok = store(i + 2, fr2, fc2))) break;
     }
     // ------------------------------------------------ epilogue
     // warp w reads TMEM lanes 32 (w % 4) .. +31 (its quadrant), column
