@@ -298,12 +298,17 @@ static int forward_impl(const dcn_conv_desc* d, const void* input, const void* w
   const size_t need = simt_forward_workspace(g);
   if (workspace_bytes < need || (need && !workspace))
     return fail(DCN_ERR_WORKSPACE, "forward workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+  // training: the columns go to the saved state (the backward's weight
+  // gradient reads them there) instead of the workspace
+  const size_t need_saved = saved ? simt_saved_columns_bytes(g) : 0;
+  if (saved && saved_bytes < need_saved)
+    return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", need_saved, saved_bytes);
+  void* cols = saved && need_saved ? saved : (need ? workspace : nullptr);
   cudaError_t e = cudaSuccess;
   dispatch_dtype(d->dtype, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     e = simt_forward<T>(g, (const T*)input, (const T*)weight, (const T*)offset,
-                        (const T*)(d->use_mask ? mask : nullptr), (const T*)bias, (T*)output,
-                        need ? workspace : nullptr, st);
+                        (const T*)(d->use_mask ? mask : nullptr), (const T*)bias, (T*)output, cols, st);
     return 0;
   });
   return e == cudaSuccess ? ok() : cuda_fail(e, "deform_conv2d_forward");
@@ -319,7 +324,9 @@ int dcn_deform_conv2d_forward(const dcn_conv_desc* d, const void* input, const v
 size_t dcn_saved_state_bytes(const dcn_conv_desc* d) {
   if (validate(d) != DCN_OK) return 0;
   const Geom g = make_geom(*d);
-  return tc_backward_supported(*d, g) ? saved_layout(g).total : 0;
+  if (tc_backward_supported(*d, g)) return saved_layout(g).total;
+  // both passes on the SIMT kernels: the forward's fp32 columns
+  return tc_forward_supported(*d, g) ? 0 : simt_saved_columns_bytes(g);
 }
 
 int dcn_deform_conv2d_forward_train(const dcn_conv_desc* d, const void* input, const void* weight,
@@ -466,6 +473,12 @@ static int backward_impl(const dcn_conv_desc* d, const void* grad_output, const 
   ws.gacc = (float*)(base + L.gin32);
   ws.gw32 = f32 ? nullptr : (float*)(base + L.gw32);
   ws.goff_scratch = base + L.goff;
+  if (saved) {
+    const size_t need_saved = simt_saved_columns_bytes(g);
+    if (saved_bytes < need_saved)
+      return fail(DCN_ERR_WORKSPACE, "saved state too small: need %zu bytes, got %zu", need_saved, saved_bytes);
+    if (need_saved) ws.cols = static_cast<const float*>(saved);
+  }
   cudaError_t e = cudaSuccess;
   dispatch_dtype(d->dtype, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;

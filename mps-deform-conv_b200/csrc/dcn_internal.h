@@ -7,16 +7,21 @@ namespace dcn {
 
 // Scratch buffers of the SIMT backward (all fp32, caller-provided).
 struct SimtBackwardWs {
-  float* gcol;          // [C*T][P] column gradient
-  float* gin32;         // [B][C][H][W] fp32 grad_input accumulator (NULL when T is float)
-  float* gacc;          // [B][H][W][C] fp32 channels-last grad_input accumulator, or NULL
-  float* gw32;          // [Co][C/G*T] fp32 grad_weight accumulator (NULL when T is float)
-  void* goff_scratch;   // offset-grad sink when the caller wants only grad_mask
+  float* gcol = nullptr;          // [C*T][P] column gradient
+  float* gin32 = nullptr;         // [B][C][H][W] fp32 grad_input accumulator (NULL when T is float)
+  float* gacc = nullptr;          // [B][H][W][C] fp32 channels-last grad_input accumulator, or NULL
+  float* gw32 = nullptr;          // [Co][C/G*T] fp32 grad_weight accumulator (NULL when T is float)
+  void* goff_scratch = nullptr;   // offset-grad sink when the caller wants only grad_mask
+  const float* cols = nullptr;    // the forward's fp32 columns [C*T][P] (training state), or NULL
 };
 
 // Forward workspace: the K-split partial sums when the output tiles alone
 // would not fill one wave of the 148 SMs (0 otherwise).
 size_t simt_forward_workspace(const Geom& g);
+// Training state of the SIMT path: the forward's fp32 columns [C*T][P] of the
+// whole batch, kept for the weight-gradient GEMM, when they fit the forward's
+// single column slice (1 GiB); 0 otherwise.
+size_t simt_saved_columns_bytes(const Geom& g);
 template <typename T>
 cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
                          const T* bias, T* out, void* workspace, cudaStream_t st);

@@ -431,6 +431,10 @@ static size_t simt_fwd_cols_bytes(const Geom& g) {
 
 size_t simt_forward_workspace(const Geom& g) { return ws_align(simt_fwd_cols_bytes(g)); }
 
+size_t simt_saved_columns_bytes(const Geom& g) {
+  return g.B > 0 && simt_fwd_slice_images(g) == g.B ? ws_align(simt_fwd_cols_bytes(g)) : 0;
+}
+
 // ---------------------------------------------------------------- host side
 template <typename T>
 cudaError_t simt_forward(const Geom& g, const T* x, const T* w, const T* off, const T* msk,
@@ -527,14 +531,16 @@ cudaError_t simt_backward(const Geom& g, const T* go, const T* x, const T* w, co
     if ((e = cudaMemsetAsync(gw32, 0, sizeof(float) * (size_t)g.Co * Kg, st)) != cudaSuccess) return e;
     GradOutLoaderPM<T> la(g, go);
     AtomicWeightEpilogue ep{gw32, g.Cog, Kg};
-    // the columns, one sample per (pixel, tap, offset group), in the column
-    // gradient's buffer (free until the dgrad GEMM below writes it)
-    {
+    // the forward's columns when it kept them, else gathered again into the
+    // column gradient's buffer (free until the dgrad GEMM below writes it)
+    const float* cols = ws.cols;
+    if (!cols) {
       KernelScope ks("im2col_og", st);
       im2col_og_kernel<T, float><<<grid_for(im2col_threads(g)), 256, 0, st>>>(g, x, off, msk, ws.gcol);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      cols = ws.gcol;
     }
-    ColumnBufferLoaderPK lb(ws.gcol, Kg, g.P);
+    ColumnBufferLoaderPK lb(cols, Kg, g.P);
     if ((e = launch_gemm<true, true>("tf32_wgrad_gemm", la, lb, ep, g.Cog, Kg, (int)g.P, g.G, true, st)) !=
         cudaSuccess)
       return e;

@@ -169,6 +169,44 @@ def test_fp32_tensor_core_gemms_vs_oracle(shape, cuda):
         assert_close(gv, rv, "float32", nm)
 
 
+def test_fp32_training_state_keeps_the_columns(cuda):
+    """fp32 problems keep the forward's fp32 columns as the training state
+    (dcn_saved_state_bytes = the column bytes); the backward's weight gradient
+    reads them instead of gathering again, bitwise the same as with the cache
+    off, and matches the oracle."""
+    from mps_deform_conv import _abi
+    import mps_deform_conv as mdc
+    B, C, H, W, Co = 2, 48, 10, 12, 40
+    g = torch.Generator().manual_seed(61)
+    x = torch.randn(B, C, H, W, generator=g)
+    w = torch.randn(Co, C, 3, 3, generator=g) / np.sqrt(C * 9)
+    off = torch.randn(B, 18, H, W, generator=g) * 1.5
+    m = torch.sigmoid(torch.randn(B, 9, H, W, generator=g))
+    b = torch.randn(Co, generator=g) * 0.1
+    go = torch.randn(B, Co, H, W, generator=g)
+    d = _abi.desc_for(x, w, off, (1, 1), (1, 1), (1, 1), m)
+    assert _abi.load().dcn_saved_state_bytes(ctypes.byref(d)) == (4 * C * 9 * B * H * W + 255) // 256 * 256
+    runs = []
+    try:
+        for cache in (True, False):
+            mdc.set_training_cache(cache)
+            leaves = [t.to(cuda).requires_grad_(True) for t in (x, off, w, b, m)]
+            out = mdc.deform_conv2d(leaves[0], leaves[1], leaves[2], leaves[3], 1, 1, 1, leaves[4])
+            runs.append([out] + list(torch.autograd.grad(out, leaves, go.to(cuda))))
+    finally:
+        mdc.set_training_cache(True)
+    # output, grad_offset and grad_mask are computed in a fixed order: bitwise
+    # equal; grad_input and grad_weight are accumulated with atomics
+    for i in (0, 2, 5):
+        assert torch.equal(runs[0][i], runs[1][i])
+    for i in (1, 3, 4):
+        assert rel_err(runs[0][i].double().cpu().numpy(), runs[1][i].double().cpu().numpy()) < 1e-6
+    refs = oracle.backward(go.double(), x.double(), off.double(), w.double(), (1, 1), (1, 1), (1, 1),
+                           m.double(), True)
+    for nm, gv, rv in zip(("grad_input", "grad_offset", "grad_weight", "grad_bias", "grad_mask"), runs[0][1:], refs):
+        assert_close(gv, rv, "float32", nm)
+
+
 def test_device_status_clean_after_runs(cuda):
     import mps_deform_conv as mdc
     mdc._get_lib().device_status()
