@@ -421,6 +421,8 @@ struct DgradArgs {
   int kb;            // 64-channel blocks of the reduction over output channels
   int b_stages;
   uint32_t idesc;
+  int tpc;           // pixel tiles per CTA, run back to back (>1 only for SW = 8)
+  int ntiles;        // pixel tiles of the problem
 };
 
 // Per-warp epilogue scratch: a 16-channel gcol slab of the warp's 32 rows and
@@ -486,7 +488,7 @@ __host__ __device__ inline DgradSmem dgrad_smem(int kb, int b_stages, int sw) {
                                             : sw == 32 ? sizeof(DgWarpSmem32)
                                             : sw == 8  ? sizeof(DgWarpSmemQ)
                                                        : sizeof(DgWarpSmem));
-  L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 1) * 8 + 16;
+  L.total = L.bar + (1 + 2 * b_stages + 2 * D_NBUF + 2) * 8 + 16;
   return L;
 }
 
@@ -522,21 +524,30 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   auto d_full = [&](int e) { return bar0 + 8u * (1 + 2 * S + e); };
   auto d_empty = [&](int e) { return bar0 + 8u * (1 + 2 * S + D_NBUF + e); };
   const uint32_t drain = bar0 + 8u * (1 + 2 * S + 2 * D_NBUF);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (1 + 2 * S + 2 * D_NBUF + 1) * 8);
+  const uint32_t a_empty = bar0 + 8u * (2 + 2 * S + 2 * D_NBUF);  // a tile's MMAs are done with A
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + (1 + 2 * S + 2 * D_NBUF + 2) * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, grp = blockIdx.y;
+  // pixel tiles tile0 .. tile0 + ntile - 1, one after the other: chunk i of
+  // the CTA is K chunk kc_lo + i % nkc_cta of tile tile0 + i / nkc_cta (the
+  // TMEM buffers keep cycling across the tiles, so the epilogue groups stay
+  // evenly loaded when a tile has few chunks)
+  const int tile0 = blockIdx.x * a.tpc, grp = blockIdx.y;
+  const int ntile = min(a.tpc, a.ntiles - tile0);
+  const int tile = tile0;  // single-tile epilogues (tpc = 1)
   // this CTA's share of the K chunks (several CTAs per tile balance the waves
   // when there are few tiles)
   const int kc_lo = (int)(((long long)a.nkc * blockIdx.z) / gridDim.z);
   const int nkc_cta = (int)(((long long)a.nkc * (blockIdx.z + 1)) / gridDim.z) - kc_lo;
+  const int nchunks = ntile * nkc_cta;
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
     for (int s = 0; s < S; ++s) { mbar_init(b_full(s), 1); mbar_init(b_empty(s), 1); }
     for (int e = 0; e < D_NBUF; ++e) { mbar_init(d_full(e), 1); mbar_init(d_empty(e), 4); }  // one per warp
     mbar_init(drain, 1);
+    mbar_init(a_empty, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -728,20 +739,24 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
     const T* msk = static_cast<const T*>(a.msk);
     const int e = warp >> 2, q = warp & 3;
     DgWarpSmemQ* ws = reinterpret_cast<DgWarpSmemQ*>(smem + L.epi) + warp;
-    {
-      const PixelCtx pc = pixel_ctx(g, (long long)tile * BM + q * 32 + lane);
-      ws->pix[lane] = make_int4(pc.valid ? pc.b : -1, pc.p, pc.y0, pc.x0);
-    }
     const int j8 = lane & 7, rsub = lane >> 3;
     const int W1 = g.W + 1, OG = g.C / 8;
     bool ok = true;
-    for (int i = e; i < nkc_cta; i += D_NBUF) {
+    int cur_tile = -1;
+    for (int i = e; i < nchunks; i += D_NBUF) {
       const bool ready = ok && mbar_wait(d_full(e), (i / D_NBUF) & 1, abort_flag, a.status, ST_D_EPI);
       ok = __all_sync(0xffffffffu, ready);
       if (!ok) break;
       tc_fence_after();
+      if (i / nkc_cta != cur_tile) {
+        // the warp's 32 pixels of this chunk's tile (the previous chunk's
+        // reads of them ended at its closing __syncwarp)
+        cur_tile = i / nkc_cta;
+        const PixelCtx pc = pixel_ctx(g, (long long)(tile0 + cur_tile) * BM + q * 32 + lane);
+        ws->pix[lane] = make_int4(pc.valid ? pc.b : -1, pc.p, pc.y0, pc.x0);
+      }
       KWalk kw;
-      kw.start(g, kc_lo + i);
+      kw.start(g, kc_lo + i % nkc_cta);
       const int cbase = grp * g.Cig + kw.cc * BK;
       const int o = cbase / 8 + j8;  // the lane's offset group
       // ---- phase 1: row owner
@@ -1222,9 +1237,12 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   } else if (warp == D_MMA_WARP) {
     // -------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(a_full, 0, abort_flag, a.status, ST_D_MMA);
+      bool ok = true;
       int committed = 0;
-      for (int i = 0; i < nkc_cta && ok; ++i) {
+      for (int i = 0; i < nchunks && ok; ++i) {
+        const int li = i % nkc_cta;
+        if (li == 0) ok = mbar_wait(a_full, (i / nkc_cta) & 1, abort_flag, a.status, ST_D_MMA);  // the tile's gOt
+        if (!ok) break;
         const int e = i % D_NBUF;
         ok = mbar_wait(d_empty(e), ((i / D_NBUF) & 1) ^ 1, abort_flag, a.status, ST_D_MMA);
         for (int kb = 0; kb < a.kb && ok; ++kb) {
@@ -1242,7 +1260,10 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
           mma_commit(b_empty(s));
           ++committed;
         }
-        if (ok) mma_commit(d_full(e));
+        if (ok) {
+          mma_commit(d_full(e));
+          if (li == nkc_cta - 1) mma_commit(a_empty);  // the loader may replace the gOt tile
+        }
       }
       if (!ok && committed > 0) {
         mma_commit(drain);
@@ -1252,23 +1273,31 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   } else {
     // -------------------------------------------- loader: gOt tile (TMA) + W^T tiles (bulk)
     if (lane == 0) {
-      mbar_arrive_expect_tx(a_full, (uint32_t)a.kb * A_STAGE_BYTES);
-      for (int cb = 0; cb < a.kb; ++cb)
-        tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, tile * BM, a_full);
-      // K blocks of W^T in order (kc, kb): block j = kc*KB + kb
+      // K blocks of W^T in order (kc, kb): block j = kc*KB + kb, the same run for every tile
       const uint8_t* wbase = static_cast<const uint8_t*>(a.wdt) +
                              ((size_t)grp * a.nkc + kc_lo) * a.kb * L.b_stage;
-      int issued = 0;
-      for (int j = 0; j < nkc_cta * a.kb; ++j) {
-        const int s = j % S;
-        if (!mbar_wait(b_empty(s), ((j / S) & 1) ^ 1, abort_flag, a.status, ST_D_LOAD)) break;
-        mbar_arrive_expect_tx(b_full(s), L.b_stage);
-        bulk_g2s(sbase + L.b + s * L.b_stage, wbase + (size_t)j * L.b_stage, L.b_stage, b_full(s));
-        ++issued;
+      const int per_tile = nkc_cta * a.kb;
+      int issued = 0, a_loads = 0;
+      bool ok = true;
+      for (int tl = 0; tl < ntile && ok; ++tl) {
+        // the previous tile's MMAs have finished reading its gOt tile
+        if (tl > 0 && !(ok = mbar_wait(a_empty, (tl - 1) & 1, abort_flag, a.status, ST_D_LOAD))) break;
+        mbar_arrive_expect_tx(a_full, (uint32_t)a.kb * A_STAGE_BYTES);
+        for (int cb = 0; cb < a.kb; ++cb)
+          tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, (tile0 + tl) * BM, a_full);
+        ++a_loads;
+        for (int jj = 0; jj < per_tile; ++jj) {
+          const int j = tl * per_tile + jj, s = j % S;
+          if (!(ok = mbar_wait(b_empty(s), ((j / S) & 1) ^ 1, abort_flag, a.status, ST_D_LOAD))) break;
+          mbar_arrive_expect_tx(b_full(s), L.b_stage);
+          bulk_g2s(sbase + L.b + s * L.b_stage, wbase + (size_t)jj * L.b_stage, L.b_stage, b_full(s));
+          ++issued;
+        }
       }
+      // copies still in flight land before the CTA exits
       for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
         mbar_wait(b_full(i % S), (i / S) & 1, abort_flag, a.status, ST_D_LOAD);
-      mbar_wait(a_full, 0, abort_flag, a.status, ST_D_LOAD);
+      if (a_loads > 0) mbar_wait(a_full, (a_loads - 1) & 1, abort_flag, a.status, ST_D_LOAD);
     }
   }
 
@@ -1783,9 +1812,17 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       const double eff = waves / std::ceil(waves);
       if (eff > best + 0.05) { best = eff; ksplit = k; }
     }
+    // corner-quad epilogue: 2 or 4 pixel tiles per CTA, back to back, while
+    // that still leaves two waves of CTAs, so that the 4 TMEM buffers'
+    // epilogue groups share a CTA's chunks evenly (9 chunks of one tile
+    // would give one group 3 and the others 2)
+    a.ntiles = n_tiles;
+    a.tpc = 1;
+    if (sw == 8 && ksplit == 1 && nkc % D_NBUF != 0)
+      while (a.tpc < 4 && (long long)((n_tiles + 2 * a.tpc - 1) / (2 * a.tpc)) * g.G >= 2 * 148) a.tpc *= 2;
     {
       KernelScope ks("dcn_dgrad_tc", st);
-      kern<<<dim3(n_tiles, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
+      kern<<<dim3((n_tiles + a.tpc - 1) / a.tpc, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (a.gq32) {  // grad_input (channels-last fp32) = the accumulator's four roles
