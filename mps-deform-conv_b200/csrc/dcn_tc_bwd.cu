@@ -1803,14 +1803,19 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
                          : dcn_dgrad_tc_kernel<T, 16>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
       return e;
-    // split the K chunks of a tile over ksplit CTAs when that fills the last
-    // wave of 148 SMs (one CTA per SM) better; keep >= 4 chunks per CTA
+    // split the K chunks of a tile over ksplit CTAs (>= 4 chunks each) when
+    // that shortens the launch: one CTA per SM, so the launch takes
+    // ceil(CTAs / 148) waves, and a CTA takes about one chunk time per chunk
+    // of its busiest TMEM buffer group (the chunks go round-robin over the 4
+    // buffers) plus about half of one for its prologue and last epilogue
+    // (measured on the c5 layer at 8, 16 and 64 images per GPU)
     int ksplit = 1;
-    double best = 0.0;
+    long long best = -1;
     for (int k = 1; k <= 6 && nkc / k >= 4; ++k) {
-      const double waves = (double)n_tiles * g.G * k / 148.0;
-      const double eff = waves / std::ceil(waves);
-      if (eff > best + 0.05) { best = eff; ksplit = k; }
+      const long long waves = ((long long)n_tiles * g.G * k + 147) / 148;
+      const int chunks = (nkc + k - 1) / k;
+      const long long cost = waves * (2 * ((chunks + D_NBUF - 1) / D_NBUF) + 1);  // in half chunk times
+      if (best < 0 || cost < best) { best = cost; ksplit = k; }
     }
     // corner-quad epilogue: 2 or 4 pixel tiles per CTA, back to back, while
     // that still leaves two waves of CTAs, so that the 4 TMEM buffers'
