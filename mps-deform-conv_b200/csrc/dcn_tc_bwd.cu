@@ -529,12 +529,15 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
   volatile int* abort_flag = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // pixel tiles tile0 .. tile0 + ntile - 1, one after the other: chunk i of
-  // the CTA is K chunk kc_lo + i % nkc_cta of tile tile0 + i / nkc_cta (the
-  // TMEM buffers keep cycling across the tiles, so the epilogue groups stay
-  // evenly loaded when a tile has few chunks)
-  const int tile0 = blockIdx.x * a.tpc, grp = blockIdx.y;
-  const int ntile = min(a.tpc, a.ntiles - tile0);
+  // pixel tiles blockIdx.x + tl * gridDim.x (tl < ntile), one after the
+  // other: chunk i of the CTA is K chunk kc_lo + i % nkc_cta of the CTA's
+  // tile i / nkc_cta (the TMEM buffers keep cycling across the tiles, so the
+  // epilogue groups stay evenly loaded when a tile has few chunks).  The CTAs
+  // of a wave work on neighbouring tiles at any one time, as with one tile
+  // per CTA, which keeps the scatter's target lines in L2.
+  const int tile0 = blockIdx.x, grp = blockIdx.y;
+  const int ntile = min(a.tpc, (a.ntiles - tile0 + (int)gridDim.x - 1) / (int)gridDim.x);
+  auto tile_of = [&](int tl) { return tile0 + tl * (int)gridDim.x; };
   const int tile = tile0;  // single-tile epilogues (tpc = 1)
   // this CTA's share of the K chunks (several CTAs per tile balance the waves
   // when there are few tiles)
@@ -752,7 +755,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         // the warp's 32 pixels of this chunk's tile (the previous chunk's
         // reads of them ended at its closing __syncwarp)
         cur_tile = i / nkc_cta;
-        const PixelCtx pc = pixel_ctx(g, (long long)(tile0 + cur_tile) * BM + q * 32 + lane);
+        const PixelCtx pc = pixel_ctx(g, (long long)tile_of(cur_tile) * BM + q * 32 + lane);
         ws->pix[lane] = make_int4(pc.valid ? pc.b : -1, pc.p, pc.y0, pc.x0);
       }
       KWalk kw;
@@ -1284,7 +1287,7 @@ dcn_dgrad_tc_kernel(const DgradArgs a, const __grid_constant__ CUtensorMap tmap_
         if (tl > 0 && !(ok = mbar_wait(a_empty, (tl - 1) & 1, abort_flag, a.status, ST_D_LOAD))) break;
         mbar_arrive_expect_tx(a_full, (uint32_t)a.kb * A_STAGE_BYTES);
         for (int cb = 0; cb < a.kb; ++cb)
-          tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, (tile0 + tl) * BM, a_full);
+          tma_load_2d(sbase + L.a + cb * A_STAGE_BYTES, &tmap_go, grp * g.Cog + cb * 64, tile_of(tl) * BM, a_full);
         ++a_loads;
         for (int jj = 0; jj < per_tile; ++jj) {
           const int j = tl * per_tile + jj, s = j % S;
