@@ -108,14 +108,24 @@ to_channels_last16_kernel(const T* __restrict__ src, T* __restrict__ dst, float*
   if (SUM && threadIdx.x < TP && c0 + (int)threadIdx.x < C) atomicAdd(gsum + c0 + threadIdx.x, csum[threadIdx.x]);
 }
 
-// fp32 src [B][HW][C] -> dst [B][C][HW] in 16-bit T (round to nearest).
-template <typename T>
+// Reader of a channels-last fp32 tensor [B][HW][C]: channels c..c+3 of pixel
+// hw of image b as one float4.
+struct NhwcF32Reader {
+  const float* src;
+  int C, HW;
+  __device__ __forceinline__ float4 operator()(int b, int hw, int c) const {
+    return *reinterpret_cast<const float4*>(src + ((long long)b * HW + hw) * C + c);
+  }
+};
+
+// fp32 [B][HW][C] (read through rd, e.g. NhwcF32Reader) -> dst [B][C][HW]
+// in 16-bit T (round to nearest).
+template <typename T, class RD>
 __global__ void __launch_bounds__(LAYOUT_THREADS)
-from_channels_last_f32_16_kernel(const float* __restrict__ src, T* __restrict__ dst, int C, int HW) {
+from_channels_last_f32_16_kernel(const RD rd, T* __restrict__ dst, int C, int HW) {
   static_assert(sizeof(T) == 2, "16-bit element types only");
   __shared__ uint32_t tile[TP][TP / 2 + 1];  // [channel][pixel pair]
   const int b = blockIdx.z, c0 = blockIdx.y * TP, hw0 = blockIdx.x * TP;
-  const float* s = src + (long long)b * HW * C;
   // 32 pixel pairs x 16 groups of 4 channels; a warp takes 4 pixel pairs x
   // 8 groups (128 contiguous bytes of each of 8 pixel rows).
   constexpr int ITERS = (TP / 2) * (TP / 4) / LAYOUT_THREADS;
@@ -127,8 +137,8 @@ from_channels_last_f32_16_kernel(const float* __restrict__ src, T* __restrict__ 
     const int hw = hw0 + 2 * hp, c = c0 + 4 * q;
     v0[it] = v1[it] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (hw < HW && c < C) {  // C % 4 == 0 and HW even: both vectors are whole
-      v0[it] = *reinterpret_cast<const float4*>(s + (long long)hw * C + c);
-      v1[it] = *reinterpret_cast<const float4*>(s + (long long)(hw + 1) * C + c);
+      v0[it] = rd(b, hw, c);
+      v1[it] = rd(b, hw + 1, c);
     }
   }
 #pragma unroll

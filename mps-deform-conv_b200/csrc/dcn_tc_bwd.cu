@@ -1344,6 +1344,28 @@ __global__ void quad_sum_kernel(const float* __restrict__ gq, float* __restrict_
   dst[1] = hi;
 }
 
+// Reader for the NHWC -> NCHW pass that takes grad_input straight from the
+// fp32 corner-quad accumulator: channels c..c+3 (one half of offset group
+// c/8) of pixel (y, x) = corner 00 of record (y, x) + (corner 01 of (y, x-1)
+// + corner 10 of (y-1, x) + corner 11 of (y-1, x-1)), summed in quad_sum's
+// order, so the result is bitwise quad_sum's followed by the plain pass.
+struct QuadSumReader {
+  const float* gq;
+  int H, W, C;
+  __device__ __forceinline__ float4 operator()(int b, int hw, int c) const {
+    const int OG = C / 8, o = c >> 3, h = (c & 7) >> 2;
+    const int y = hw / W, x = hw - y * W;
+    const long long r00 = (((long long)b * (H + 1) + y + 1) * (W + 1) + x + 1) * OG + o;
+    const long long rows = (long long)(W + 1) * OG;
+    const float4 p0 = *reinterpret_cast<const float4*>(gq + r00 * 32 + 4 * h);
+    const float4 p1 = *reinterpret_cast<const float4*>(gq + (r00 - OG) * 32 + 8 + 4 * h);
+    const float4 p2 = *reinterpret_cast<const float4*>(gq + (r00 - rows) * 32 + 16 + 4 * h);
+    const float4 p3 = *reinterpret_cast<const float4*>(gq + (r00 - rows - OG) * 32 + 24 + 4 * h);
+    return make_float4(p0.x + (p1.x + p2.x + p3.x), p0.y + (p1.y + p2.y + p3.y), p0.z + (p1.z + p2.z + p3.z),
+                       p0.w + (p1.w + p2.w + p3.w));
+  }
+};
+
 // ================================================================ prep / finalize
 // grad_output NCHW [B][Co][HWo] -> gOt [B*HWo][Co]; gb32[co] += tile sums.
 template <typename T>
@@ -1760,6 +1782,7 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
     convert_multi_kernel<T><<<1, 256, 0, st>>>(jobs);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  const float* gq_fused = nullptr;  // corner-quad accumulator summed by the final NCHW pass
   if (need_d) {
     if (saved) {  // the forward built it with the training state
       wdt = reinterpret_cast<T*>(const_cast<char*>(static_cast<const char*>(saved)) + SV.wdt);
@@ -1833,7 +1856,11 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
       kern<<<dim3((n_tiles + a.tpc - 1) / a.tpc, g.G, ksplit), D_NTHREADS, smem, st>>>(a, tmap);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (a.gq32) {  // grad_input (channels-last fp32) = the accumulator's four roles
+    // grad_input = the accumulator's four roles: summed inside the final
+    // NCHW pass below, or here (channels-last grad_input, unaligned pointers)
+    if (a.gq32 && !g.in_nhwc && layout::from_channels_last_vec_ok(gi32, gin, g.C, (long long)g.H * g.W)) {
+      gq_fused = a.gq32;
+    } else if (a.gq32) {
       KernelScope ks("quad_sum", st);
       const long long n = (long long)g.B * g.H * g.W * (g.C / 8);
       quad_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.gq32, gi32, g.H, g.W, g.C, n);
@@ -1850,9 +1877,12 @@ cudaError_t tc_backward_t(const Geom& g, const T* go, const T* x, const T* w, co
   if (gin && !g.in_nhwc) {
     KernelScope ks("grad_input_to_nchw", st);
     const dim3 grid = layout::tile_grid(g.C, (long long)g.H * g.W, g.B);
-    if (layout::from_channels_last_vec_ok(gi32, gin, g.C, (long long)g.H * g.W))
+    if (gq_fused)
       layout::from_channels_last_f32_16_kernel<T><<<grid, layout::LAYOUT_THREADS, 0, st>>>(
-          gi32, gin, g.C, g.H * g.W);
+          QuadSumReader{gq_fused, g.H, g.W, g.C}, gin, g.C, g.H * g.W);
+    else if (layout::from_channels_last_vec_ok(gi32, gin, g.C, (long long)g.H * g.W))
+      layout::from_channels_last_f32_16_kernel<T><<<grid, layout::LAYOUT_THREADS, 0, st>>>(
+          layout::NhwcF32Reader{gi32, g.C, g.H * g.W}, gin, g.C, g.H * g.W);
     else
       nhwc_f32_to_nchw_kernel<T><<<grid, 256, 0, st>>>(gi32, gin, g.C, g.H * g.W);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
