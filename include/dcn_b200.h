@@ -193,9 +193,12 @@ DCN_API int dcn_deform_conv2d_backward(const dcn_conv_desc *desc, const void *gr
  * With it the backward skips the input re-layout and the column re-gather:
  * the weight-gradient GEMM streams the saved tiles.  The state costs
  * dcn_saved_state_bytes() of device memory (about B*Ho*Wo*C*kh*kw*2 bytes)
- * between the two calls; 0 means this problem keeps nothing (SIMT kernels),
- * and the _train calls then behave like the plain ones.  `saved` must not be
- * modified between the forward and the backward.
+ * between the two calls.  Problems outside the fused fp16/bf16 kernels (fp32,
+ * and shapes those kernels do not take) keep the forward's fp32 column buffer
+ * [C*kh*kw][B*Ho*Wo] instead (4 bytes per element), when it fits in 1 GiB;
+ * 0 means this problem keeps nothing, and the _train calls then behave like
+ * the plain ones.  `saved` must not be modified between the forward and the
+ * backward.
  */
 DCN_API size_t dcn_saved_state_bytes(const dcn_conv_desc *desc);
 DCN_API int dcn_deform_conv2d_forward_train(const dcn_conv_desc *desc, const void *input,
