@@ -1535,31 +1535,39 @@ wgrad_reduce_kernel(const float* __restrict__ gwp, T* __restrict__ gw, const flo
   const float4* src = reinterpret_cast<const float4*>(gwp + ((size_t)co * nkc + cc) * 64);
   for (int i = threadIdx.x; i < 16 * T_; i += WR_THREADS) {
     const size_t at = (size_t)(i >> 4) * ncc * 16 + (i & 15);  // tap i/16, float4 i%16
-    // splits s = 4j + u go to accumulator u (four loads in flight), then
-    // ((a0 + a1) + (a2 + a3)): a fixed order, so grad_weight is reproducible
-    float4 a[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-    int sp = 0;
-    for (; sp + 4 <= splits; sp += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float4 v = src[(size_t)(sp + u) * split_stride4 + at];
-        a[u].x += v.x; a[u].y += v.y; a[u].z += v.z; a[u].w += v.w;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      if (sp + u < splits) {
-        const float4 v = src[(size_t)(sp + u) * split_stride4 + at];
-        a[u].x += v.x; a[u].y += v.y; a[u].z += v.z; a[u].w += v.w;
-      }
-    }
     float4 acc;
-    acc.x = (a[0].x + a[1].x) + (a[2].x + a[3].x);
-    acc.y = (a[0].y + a[1].y) + (a[2].y + a[3].y);
-    acc.z = (a[0].z + a[1].z) + (a[2].z + a[3].z);
-    acc.w = (a[0].w + a[1].w) + (a[2].w + a[3].w);
+    if (splits < 16) {  // in split order
+      acc = src[at];
+      for (int sp = 1; sp < splits; ++sp) {
+        const float4 v = src[(size_t)sp * split_stride4 + at];
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+    } else {
+      // many splits (few K chunks, e.g. 64 channels): split s = 4j + u into
+      // accumulator u, four loads in flight, then ((a0 + a1) + (a2 + a3))
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      int sp = 0;
+      for (; sp + 4 <= splits; sp += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 v = src[(size_t)(sp + u) * split_stride4 + at];
+          a[u].x += v.x; a[u].y += v.y; a[u].z += v.z; a[u].w += v.w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        if (sp + u < splits) {
+          const float4 v = src[(size_t)(sp + u) * split_stride4 + at];
+          a[u].x += v.x; a[u].y += v.y; a[u].z += v.z; a[u].w += v.w;
+        }
+      }
+      acc.x = (a[0].x + a[1].x) + (a[2].x + a[3].x);
+      acc.y = (a[0].y + a[1].y) + (a[2].y + a[3].y);
+      acc.z = (a[0].z + a[1].z) + (a[2].z + a[3].z);
+      acc.w = (a[0].w + a[1].w) + (a[2].w + a[3].w);
+    }
     float* row = wr_tile + (i >> 4) * 65 + (i & 15) * 4;
     row[0] = acc.x; row[1] = acc.y; row[2] = acc.z; row[3] = acc.w;
   }
