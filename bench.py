@@ -432,9 +432,10 @@ def run_ours(args):
 
 def run_suite(dev, skip, steps=5, warmup=3):
     """Short device-timed fwd(+bwd) runs of the other workloads (N=1): one
-    entry per problem with ms/step, TFLOP/s, samples/s, which kernel family
-    ran it and its top kernels.  Inputs stay resident; the L2 is flushed
-    between steps.  Forward-only problems on the tensor cores get a second
+    entry per problem with ms/step (CUDA-graph replay of the step, as the
+    main timed region; the eager time beside it), TFLOP/s, samples/s, which
+    kernel family ran it and its top kernels (from the eager pass).  Inputs
+    stay resident; the L2 is flushed between steps.  Forward-only problems on the tensor cores get a second
     entry, "<name>/frozen_cl": the same call as a channels_last network in
     inference makes it (input already channels_last, weights frozen, so the
     forward weight image is built once: set_weight_image_cache)."""
@@ -470,11 +471,36 @@ def run_suite(dev, skip, steps=5, warmup=3):
         _abi.profile_enable(False)
         prof = sorted(_abi.profile_summary(), key=lambda r: -r[2])
         ms /= steps
+        eager_ms = ms
+        # the step's device time without host launch gaps: captured once in a
+        # CUDA graph and replayed, as the main timed region does
+        timing = "eager steps"
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            torch.cuda.synchronize()
+            tot = 0.0
+            for _ in range(steps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                graph.replay()
+                b.record()
+                torch.cuda.synchronize()
+                tot += a.elapsed_time(b)
+            ms = tot / steps
+            timing = "CUDA-graph replay"
+            del graph
+            torch.cuda.synchronize()
+        except Exception as exc:  # keep the eager time
+            print(f"[bench] {p.name}: graph capture failed, eager time kept: {exc}", file=sys.stderr)
         tc = bool(mdc._get_lib().uses_tensor_cores(inp["input"], inp["weight"], p.stride, p.stride, p.padding,
                                                    p.padding, p.dilation, p.dilation, p.groups,
                                                    p.offset_groups, p.use_mask))
         return tc, {"description": p.description, "pass": "fwd+bwd" if p.training else "fwd",
-                    "ms_per_step": round(ms, 4), "tflops": round(p.flops() / (ms / 1e3) / 1e12, 3),
+                    "ms_per_step": round(ms, 4), "timing": timing, "eager_ms_per_step": round(eager_ms, 4),
+                    "tflops": round(p.flops() / (ms / 1e3) / 1e12, 3),
                     "samples_per_s": round(p.batch / (ms / 1e3), 1),
                     "min_hbm_bytes": p.min_hbm_bytes(),
                     "hbm_frac_of_measured": round(p.min_hbm_bytes() / (ms / 1e3) / 1e9 / load_peaks()["hbm_gbs"], 4),
