@@ -362,7 +362,8 @@ DCN_API int dcn_device_status(void *stream);
  * corner, 3 tensor-core gather input vector, 4 offset element, 5 mask
  * element, 6 corner-quad record, 7 dgrad corner vector, 8 dgrad grad_input
  * reduction, 9 corner-quad reduction, 10 offset/mask gradient element,
- * 11 SIMT col2im, 12 SIMT channels-last col2im, 13 SIMT im2col column.
+ * 11 general-path col2im, 12 general-path channels-last col2im, 13
+ * general-path im2col column.
  */
 typedef struct dcn_bounds_record {
   uint64_t count;         /* indices found outside their tensor */
@@ -372,8 +373,10 @@ typedef struct dcn_bounds_record {
 DCN_API int dcn_debug_bounds_enabled(void);
 DCN_API int dcn_debug_bounds_read(dcn_bounds_record *out, int reset);
 
-/* Which implementation a descriptor runs on: 1 = tensor-core (tcgen05)
- * kernels, 0 = general SIMT kernels (any shape, fp32 path). */
+/* Which implementation a descriptor runs on: 1 = the fused fp16/bf16
+ * tensor-core (tcgen05) kernels, 0 = the general path (any shape, the fp32
+ * path: materialized columns, GEMMs on tcgen05 tf32 MMAs, CUDA-core gather
+ * and scatter). */
 DCN_API int dcn_uses_tensor_cores(const dcn_conv_desc *desc);
 
 #ifdef __cplusplus
